@@ -1,0 +1,380 @@
+"""Energy + force throughput of a patched MACE model on B200 (and the CPU e3nn-path baseline).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the configuration the headline metric is quoted on): random 128-channel MACE,
+hidden 128x0e+128x1o, l_max 3, correlation 3, 4 elements (H, C, O, Pt), r_max 5 A, 2 interactions; one Pt(100) 6x6x4
+slab with seeded CO/O/H adsorbates (~160 atoms, ~5 000 edges).  With N GPUs (torchrun, one process per GPU) every
+rank runs its own structure (seed = rank): weak scaling, the only collective is the per-step energy all_gather.
+
+One step = one energy + force call (model forward + autograd backward through the patched kernels).  Inputs are
+much smaller than L2, so L2 is flushed (256 MB write) before every timed step, outside the CUDA-event interval.
+
+Printed JSON (rank 0): value = atoms x ranks / step time (max over ranks, CUDA events); e2e = the same through the
+public API with host inputs (pinned H2D copies of the graph and a D2H copy of the forces inside the timed interval);
+roofline = the dominant kernel's algorithmic bytes / its CUDA-event duration against the measured HBM copy
+bandwidth; cpu_baseline = the unpatched e3nn-path model on the host cores (rank 0, N = 1 only).
+"""
+from __future__ import annotations
+
+import argparse
+import copy
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from mace_mps_kernels_b200 import _lib, patch_model, standin  # noqa: E402
+from mace_mps_kernels_b200.conv import CudaConvTP  # noqa: E402
+from mace_mps_kernels_b200.symmetric import CudaSymmetricContraction  # noqa: E402
+
+METRIC = 'E+F atom-steps/s'
+UNIT = 'atom-steps/s'
+HIDDEN, LMAX, CORR, RMAX = '128x0e+128x1o', 3, 3, 5.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    p = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d['hbm_gbs']), 'measured'
+    return FALLBACK_HBM_GBS, 'fallback'
+
+
+def workload(rank):
+    st = standin.pt100_random(seed=rank)
+    batch = standin.structure_batch([st], standin.ELEMENTS_PTCOH, RMAX)
+    return st, batch
+
+
+def config_dict(n_atoms, n_edges, world):
+    return {'workload': f'configs[1]: MACE 128ch {HIDDEN} l_max {LMAX} corr {CORR} 4 elements r_max {RMAX}; '
+                        f'Pt(100) 6x6x4 + CO/O/H, {n_atoms} atoms, {n_edges} edges per rank',
+            'model': 'ScaleShiftMACE (in-repo mace-torch 0.3.x stand-in, random weights seed 0)',
+            'global_batch': world, 'atoms_per_rank': n_atoms, 'edges_per_rank': n_edges,
+            'parallelism': f'dp{world} (structure batch, one structure per rank)',
+            'l2': 'flushed (256 MB write) before every timed step'}
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = 'clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,' \
+             'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,' \
+             'clocks_event_reasons.sw_power_cap'
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                                          '-lms', '200', '-i', str(self.index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for l in getattr(self, 'lines', []):
+            f = [x.strip() for x in l.split(',')]
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower() == 'active':
+                    reasons.add(n)
+        return {'sm_mhz': float(np.median(sm)) if sm else None, 'sm_max_mhz': mx, 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+def flush_l2(buf):
+    buf.zero_()
+
+
+def e_and_f(model, batch):
+    b = dict(batch)
+    b['positions'] = b['positions'].detach().requires_grad_(True)
+    out = model(b, compute_force=True, training=False)
+    return out['energy'], out['forces']
+
+
+def capture_op_inputs(model, batch):
+    """Arguments every patched op sees in one E+F call (for per-op timing)."""
+    calls = []
+
+    def hook(mod, args, kwargs, out):
+        calls.append((mod, [a.detach() if torch.is_tensor(a) else a for a in args], out.detach()))
+
+    hs = [m.register_forward_hook(hook, with_kwargs=True) for m in model.modules()
+          if isinstance(m, (CudaConvTP, CudaSymmetricContraction))]
+    e_and_f(model, batch)
+    for h in hs:
+        h.remove()
+    return calls
+
+
+def conv_bytes(spec, N, E):
+    """Algorithmic bytes of one conv launch: unique tensors once (fp32) + CSR (int32) + edge index (int64)."""
+    fwd = 4 * (N * spec.x_dim + E * spec.y_dim + E * spec.w_dim + N * spec.out_dim) + 4 * (N + 1 + E) + 8 * E
+    bwd = 4 * (N * spec.out_dim + N * spec.x_dim + E * spec.y_dim + E * spec.w_dim + E * spec.w_dim
+               + E * spec.y_dim + N * spec.x_dim) + 4 * (N + 1 + E) + 8 * E
+    return fwd, bwd
+
+
+def time_ops(calls, reps, flush):
+    """CUDA-event time per launch of every patched op's forward and backward kernel (L2 flushed before each)."""
+    res = []
+    stream = torch.cuda.current_stream()
+    for mod, args, out in calls:
+        if isinstance(mod, CudaConvTP):
+            x, Y, W, ei = args
+            x, Y, W = x.clone().requires_grad_(True), Y.clone().requires_grad_(True), W.clone().requires_grad_(True)
+            kind = 'conv'
+        else:
+            x, attrs = args
+            x = x.clone().requires_grad_(True)
+            kind = 'sc'
+        g = torch.randn_like(out)
+        tf, tb = [], []
+        for r in range(reps + 2):
+            flush(stream)
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record()
+            o = mod(x, Y, W, ei) if kind == 'conv' else mod(x, attrs)
+            e1.record()
+            flush(stream)
+            e1b = torch.cuda.Event(enable_timing=True)
+            e1b.record()
+            torch.autograd.backward(o, g)
+            e2.record()
+            torch.cuda.synchronize()
+            if r >= 2:
+                tf.append(e0.elapsed_time(e1))
+                tb.append(e1b.elapsed_time(e2))
+            x.grad = None
+            if kind == 'conv':
+                Y.grad = W.grad = None
+        N = x.shape[0]
+        if kind == 'conv':
+            E = Y.shape[0]
+            bf, bb = conv_bytes(mod.spec, N, E)
+            res.append(dict(op=f'conv_tp L={mod.spec.x_dim // mod.spec.mul}', kind=kind, N=N, E=E,
+                            fwd_us=1e3 * float(np.mean(tf)), bwd_us=1e3 * float(np.mean(tb)), fwd_bytes=bf,
+                            bwd_bytes=bb))
+        else:
+            ff, fb = mod.spec.flops()
+            C = mod.spec.C
+            res.append(dict(op=f'symcon out_dim={mod.spec.out_dim}', kind=kind, N=N, fwd_us=1e3 * float(np.mean(tf)),
+                            bwd_us=1e3 * float(np.mean(tb)), fwd_flops=ff * N * C, bwd_flops=fb * N * C))
+    return res
+
+
+def cpu_baseline(n_steps_cap=5, budget_s=20.0):
+    """Unpatched (e3nn-path) stand-in model on the host cores: E+F atom-steps/s on this rank's structure."""
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    model = standin.make_model(HIDDEN, LMAX, CORR, seed=0, elements=standin.ELEMENTS_PTCOH)
+    st, batch = workload(0)
+    e_and_f(model, batch)                       # warm-up (allocations, caches)
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < n_steps_cap and time.perf_counter() - t_start < budget_s:
+        t0 = time.perf_counter()
+        e_and_f(model, batch)
+        times.append(time.perf_counter() - t0)
+    sec = float(np.mean(times))
+    return {'value': len(st) / sec, 'unit': UNIT, 'cores': cores, 'kind': 'port',
+            'sample': f'{len(times)} E+F calls of the unpatched model (e3nn-style materialise-then-index_add conv, '
+                      f'einsum symmetric contraction), fp32, {len(st)} atoms, {sec * 1e3:.0f} ms each'}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--op-reps', type=int, default=10)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+
+    if a.impl == 'reference':
+        return reference_arm(a, rank, world)
+
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    torch.manual_seed(0)
+    model = standin.make_model(HIDDEN, LMAX, CORR, seed=0, elements=standin.ELEMENTS_PTCOH).to(dev)
+    rep = patch_model(model, verbose=False)
+    assert len(rep['patched']) == 4, rep
+    st, host_batch = workload(rank)
+    n_atoms, n_edges = len(st), int(host_batch['edge_index'].shape[1])
+    batch = standin.to_device(host_batch, dev)
+    flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    e_all = torch.zeros(world, device=dev)
+
+    def step(b):
+        E, F = e_and_f(model, b)
+        if dist is not None:
+            dist.all_gather_into_tensor(e_all, E.detach().reshape(1))
+        return E, F
+
+    for _ in range(a.warmup):
+        step(batch)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+
+    # ---- device-resident inputs -------------------------------------------------------------------------------
+    _lib.LAUNCHES.clear()
+    evs = []
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        for _ in range(a.steps):
+            flush_l2(flush_buf)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            step(batch)
+            e1.record()
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+    launches = sum(_lib.LAUNCHES.values())
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / a.steps
+    ms_t = torch.tensor([ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+
+    # ---- end to end through the public API with host buffers ----------------------------------------------------
+    pinned = {k: (v.pin_memory() if torch.is_tensor(v) else v) for k, v in host_batch.items()}
+    h2d = sum(v.numel() * v.element_size() for v in pinned.values() if torch.is_tensor(v))
+    forces_host = torch.empty(n_atoms, 3).pin_memory()
+    d2h = forces_host.numel() * 4 + 4
+    evs = []
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    for _ in range(a.steps):
+        flush_l2(flush_buf)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        b = {k: (v.to(dev, non_blocking=True) if torch.is_tensor(v) else v) for k, v in pinned.items()}
+        E, F = step(b)
+        forces_host.copy_(F, non_blocking=True)
+        e_host = E.detach().to('cpu', non_blocking=True)
+        e1.record()
+        evs.append((e0, e1))
+        e1.synchronize()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    ms_e2e = sum(e0.elapsed_time(e1) for e0, e1 in evs) / a.steps
+    t = torch.tensor([ms_e2e], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_e2e = float(t.item())
+
+    # ---- per-op kernel timing (dominant kernel -> roofline) -----------------------------------------------------
+    calls = capture_op_inputs(model, batch)
+    ops = time_ops(calls, a.op_reps, lambda s: flush_l2(flush_buf))
+    hbm, hbm_kind = peaks()
+    conv_ops = [o for o in ops if o['kind'] == 'conv']
+    dom = max(conv_ops, key=lambda o: o['fwd_us'] + o['bwd_us'])
+    dom_bytes = dom['fwd_bytes'] + dom['bwd_bytes']
+    dom_us = dom['fwd_us'] + dom['bwd_us']
+    achieved = dom_bytes / (dom_us * 1e-6) / 1e9
+    roofline = {'kernel': f"{dom['op']} fwd+bwd (mmk_conv_fwd_kernel + mmk_conv_bwd_kernel)", 'bound': 'hbm',
+                'achieved': round(achieved, 1), 'peak': hbm, 'peak_kind': hbm_kind, 'unit': 'GB/s',
+                'frac': round(achieved / hbm, 4), 'traffic': None,
+                'algorithmic_bytes_per_launch': dom_bytes, 'us_per_launch': round(dom_us, 2),
+                'note': 'fits in L2 at this size: latency-bound; see profiles/ for the large-system sweep'}
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not a.no_cpu_baseline:
+            cpu = cpu_baseline()
+        res = {
+            'metric': METRIC, 'value': round(n_atoms * world / (ms * 1e-3), 1), 'unit': UNIT, 'n_gpus': world,
+            'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': round(ms, 4), 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded structures, '
+            'random-init weights of the configs[1] architecture)', 'config': config_dict(n_atoms, n_edges, world),
+            'e2e': {'value': round(n_atoms * world / (ms_e2e * 1e-3), 1), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
+                    'd2h_bytes_per_step': d2h, 'ms_per_step': round(ms_e2e, 4)},
+            'roofline': roofline, 'cpu_baseline': cpu, 'gpu_launches': launches, 'clocks': clk.summary(),
+            'ops': [{k: (round(v, 2) if isinstance(v, float) else v) for k, v in o.items()} for o in ops],
+        }
+        print(json.dumps(res))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def reference_arm(a, rank, world):
+    """The reference's path on the host cores: the unpatched e3nn-path model, E+F on the same workload (rank 0)."""
+    if rank != 0:
+        return
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    model = standin.make_model(HIDDEN, LMAX, CORR, seed=0, elements=standin.ELEMENTS_PTCOH)
+    st, batch = workload(0)
+    for _ in range(a.warmup):
+        e_and_f(model, batch)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        e_and_f(model, batch)
+    sec = (time.perf_counter() - t0) / a.steps
+    v = round(len(st) / sec, 2)
+    res = {'impl': 'reference', 'metric': METRIC, 'value': v, 'unit': UNIT, 'n_gpus': world, 'steps': a.steps,
+           'warmup': a.warmup, 'ms_per_step': round(sec * 1e3, 3), 'higher_is_better': True, 'scaling': 'weak',
+           'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+           'config': config_dict(len(st), int(batch['edge_index'].shape[1]), 1),
+           'cpu_baseline': {'value': v, 'unit': UNIT, 'cores': cores, 'kind': 'port',
+                            'sample': f'one E+F call of the unpatched e3nn-path model per step, {len(st)} atoms'},
+           'e2e': {'value': v, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(res))
+
+
+if __name__ == '__main__':
+    main()

@@ -1,0 +1,160 @@
+/*
+ * mmk.h -- C ABI of the B200 (sm_100a) MACE kernels: the interaction convolution ``conv_tp`` (gather -> channel-wise
+ * weighted uvu tensor product -> scatter-sum over receivers) and the symmetric contraction (product basis), each
+ * with forward and first-order backward, plus the receiver/sender CSR builder they run on.
+ *
+ * Conventions for every entry point:
+ *   - all tensor arguments are DEVICE pointers to contiguous row-major arrays owned by the caller; the library never
+ *     allocates tensor memory on these paths (per-layer constant tables are owned by the layer handles);
+ *   - ``stream`` is a cudaStream_t (NULL = legacy default stream); work is only enqueued, nothing synchronises;
+ *   - return value 0 (MMK_OK) on success, otherwise an MMK_ERR_* code; ``mmk_last_error()`` gives a message
+ *     (thread-local, valid until the next call from the same thread);
+ *   - fp32 data, int32 CSR arrays, int64 edge indices (PyTorch's edge_index dtype).
+ *
+ * Layouts (e3nn "mul_ir", per node / edge), MUL = channels per irrep block:
+ *   x   [N, X_DIM]        x block i (degree l_i): x_off[i] + u*(2 l_i + 1) + m
+ *   Y   [E, Y_DIM]        Y block j (multiplicity 1): y_off[j] + m
+ *   W   [E, NINS*MUL]     instruction k, channel u at k*MUL + u
+ *   out [N, OUT_DIM]      output block o: o_off[o] + u*(2 l_o + 1) + m
+ *   out[n] = sum_{e : receiver(e) = n} TP(x[sender(e)], Y[e], W[e])
+ */
+#ifndef MMK_H
+#define MMK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(MMK_BUILD)
+#define MMK_API __attribute__((visibility("default")))
+#else
+#define MMK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MMK_OK 0
+#define MMK_ERR_INVALID 1       /* bad descriptor or argument (message says which)      */
+#define MMK_ERR_COMPILE 2       /* NVRTC failed on the generated layer source             */
+#define MMK_ERR_CUDA 3          /* a CUDA runtime call failed                             */
+#define MMK_ERR_UNSUPPORTED 4   /* valid request this build does not implement            */
+
+MMK_API const char *mmk_last_error(void);
+/* library version, e.g. "0.1.0" */
+MMK_API const char *mmk_version(void);
+
+/* ------------------------------------------------------------------------------------------------------------------
+ * conv_tp layer
+ * ---------------------------------------------------------------------------------------------------------------- */
+
+/* Description of one uvu TensorProduct (what reference src/mace_mps_kernels/conv.py:133-166 ``ConvSpec`` holds).
+ * terms: the effective coefficient c of path (instruction k, x component a, Y component b, output component m),
+ * i.e. CG x normalisation x path weight exactly as the probed TensorProduct applies it. */
+typedef struct mmk_conv_desc {
+    int mul;                 /* channels per block, a multiple of 32 (reference conv.py:122)            */
+    int n_in1;               /* number of x blocks                                                      */
+    const int *in1_l;        /* [n_in1] degree of each x block, layout order                            */
+    int n_in2;               /* number of Y blocks (multiplicity 1 each)                                */
+    const int *in2_l;        /* [n_in2]                                                                 */
+    int n_out;               /* number of output blocks                                                 */
+    const int *out_l;        /* [n_out]                                                                 */
+    int nins;                /* number of instructions                                                  */
+    const int *ins_i1;       /* [nins] x block of instruction k                                         */
+    const int *ins_i2;       /* [nins] Y block                                                          */
+    const int *ins_io;       /* [nins] output block (several instructions may share one: they sum)      */
+    int nterms;              /* number of nonzero coefficients                                          */
+    const int *term_ins;     /* [nterms] instruction k                                                  */
+    const int *term_a;       /* [nterms] component of the x block, 0..2 l1                              */
+    const int *term_b;       /* [nterms] component of the Y block, 0..2 l2                              */
+    const int *term_m;       /* [nterms] component of the output block, 0..2 l3                         */
+    const double *term_c;    /* [nterms] coefficient                                                    */
+} mmk_conv_desc;
+
+typedef struct mmk_conv_layer mmk_conv_layer;
+
+/* Generates the layer's specialised sm_100a kernels (coefficients baked in as constants), compiles them with NVRTC
+ * and loads them.  Replaces ``MetalConvTP.__init__`` -> ``ConvSpec`` + ``torch.mps.compile_shader(source(spec))``
+ * (reference src/mace_mps_kernels/conv.py:356-359).  Identical descriptors share one compiled module. */
+MMK_API int mmk_conv_layer_create(const mmk_conv_desc *desc, mmk_conv_layer **layer);
+MMK_API int mmk_conv_layer_destroy(mmk_conv_layer *layer);
+/* dims of a created layer: x_dim, y_dim, out_dim, w_dim (= nins*mul) */
+MMK_API int mmk_conv_layer_dims(const mmk_conv_layer *layer, int *x_dim, int *y_dim, int *out_dim, int *w_dim);
+/* NVRTC-compile the generated source without loading it (needs no GPU); for build checks and tests. */
+MMK_API int mmk_conv_compile_check(const mmk_conv_desc *desc);
+
+/* Forward: out[n] = sum over the receiver-CSR segment of n.  Deterministic (fixed edge order), no atomics.
+ * Replaces reference conv.py:109-141 (``conv_fwd`` kernel) as launched by conv.py:325-326.
+ *   recv_rowptr [N+1], recv_eids [E] : receiver CSR (mmk_csr_build on edge_index[1])
+ *   senders [E] int64                : edge_index[0]                                                          */
+MMK_API int mmk_conv_fwd(const mmk_conv_layer *layer, const float *x, const float *Y, const float *W,
+                 const int32_t *recv_rowptr, const int32_t *recv_eids, const int64_t *senders,
+                 float *out, int64_t n_nodes, int64_t n_edges, void *stream);
+
+/* Backward (first order), fused: one pass over the sender CSR computes
+ *   gx[s]  = sum_{e: sender(e)=s} dTP/dx   (per sender, atomic-free),
+ *   gW[e], gY[e]                           (per edge; the channel sum of gY is a warp-shuffle + shared reduction).
+ * Replaces reference conv.py:144-176 (``conv_bwd_x``) and conv.py:179-222 (``conv_bwd_wy``) as launched by
+ * conv.py:340-348.  Any of gx / gY / gW may be NULL to skip that output (gY and gW are computed together). */
+MMK_API int mmk_conv_bwd(const mmk_conv_layer *layer, const float *x, const float *Y, const float *W, const float *grad_out,
+                 const int32_t *send_rowptr, const int32_t *send_eids, const int64_t *receivers,
+                 float *gx, float *gY, float *gW, int64_t n_nodes, int64_t n_edges, void *stream);
+
+/* ------------------------------------------------------------------------------------------------------------------
+ * CSR of an edge index (reference src/mace_mps_kernels/conv.py:308-314 ``csr_by``)
+ * ---------------------------------------------------------------------------------------------------------------- */
+
+/* Bytes of device workspace mmk_csr_build needs for (n_nodes, n_edges). */
+MMK_API size_t mmk_csr_workspace_bytes(int64_t n_nodes, int64_t n_edges);
+/* rowptr[n+1] and eids[E] such that eids[rowptr[v]:rowptr[v+1]] lists the edges with index[e] == v in increasing e
+ * -- exactly torch.argsort(index, stable=True) grouped by bincount/cumsum.  Out-of-range indices set *error_flag
+ * (device int, may be NULL) to 1 and are dropped.  workspace: mmk_csr_workspace_bytes() bytes, 16-byte aligned. */
+MMK_API int mmk_csr_build(const int64_t *index, int64_t n_edges, int64_t n_nodes, int32_t *rowptr, int32_t *eids,
+                  void *workspace, size_t workspace_bytes, int32_t *error_flag, void *stream);
+
+/* ------------------------------------------------------------------------------------------------------------------
+ * symmetric contraction layer
+ * ---------------------------------------------------------------------------------------------------------------- */
+
+/* Polynomial form of one MACE SymmetricContraction (reference src/mace_mps_kernels/symmetric.py:52-75 ``SCSpec``):
+ * for output block q (M_q components, output offset out_off_q = C * sum_{q'<q} M_q'), term t with monomial
+ * prod_{i in idx_t} x_i (degree deg_t, indices into the n_ell per-channel components) and first row row_t:
+ *   out[b, out_off_q + c*M_q + m] = sum_t T[elem(b), row_t + m, c] * prod_{i in idx_t} x[b, c, i]
+ * T is [n_elem, n_rows, C] fp32 on the device (caller-owned). */
+typedef struct mmk_sc_desc {
+    int C;                   /* channels                                                             */
+    int n_ell;               /* per-channel feature components, (l_max+1)^2                          */
+    int n_rows;              /* rows of T                                                            */
+    int n_blocks;            /* output blocks (one per output irrep)                                 */
+    const int *block_M;      /* [n_blocks] components per block (2L+1)                               */
+    const int *block_nterms; /* [n_blocks] terms of each block (terms are stored block after block)  */
+    int max_degree;          /* largest monomial degree (= correlation order)                        */
+    const int *term_degree;  /* [nterms] degree of term t, 1..max_degree                             */
+    const int *term_idx;     /* [nterms * max_degree] sorted component indices, padded with -1      */
+    const int *term_row;     /* [nterms] first row of T for term t                                   */
+} mmk_sc_desc;
+
+typedef struct mmk_sc_layer mmk_sc_layer;
+
+/* Compiles the specialised kernels (monomial list baked in).  Replaces ``MetalSymmetricContraction.__init__``
+ * (reference symmetric.py:161-166). */
+MMK_API int mmk_sc_layer_create(const mmk_sc_desc *desc, mmk_sc_layer **layer);
+MMK_API int mmk_sc_layer_destroy(mmk_sc_layer *layer);
+MMK_API int mmk_sc_layer_dims(const mmk_sc_layer *layer, int *C, int *n_ell, int *out_dim, int *n_rows);
+MMK_API int mmk_sc_compile_check(const mmk_sc_desc *desc);
+
+/* elem[b] = argmax_e node_attrs[b, e] (first maximum), as torch.argmax (reference symmetric.py:169). */
+MMK_API int mmk_elem_index(const float *node_attrs, int64_t n_nodes, int n_elem, int32_t *elem, void *stream);
+
+/* out[N, out_dim] from x[N, C, n_ell]; replaces reference symmetric.py:82-105 (``sc_fwd``). */
+MMK_API int mmk_sc_fwd(const mmk_sc_layer *layer, const float *x, const int32_t *elem, const float *T, float *out,
+               int64_t n_nodes, void *stream);
+/* gx[N, C, n_ell] = d(sum out*grad_out)/dx; replaces reference symmetric.py:106-131 (``sc_bwd``). */
+MMK_API int mmk_sc_bwd(const mmk_sc_layer *layer, const float *x, const int32_t *elem, const float *T,
+               const float *grad_out, float *gx, int64_t n_nodes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MMK_H */

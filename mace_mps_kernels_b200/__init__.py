@@ -1,0 +1,84 @@
+"""
+mace-b200-kernels -- fused sm_100a CUDA kernels for MACE inference on NVIDIA B200 (PyTorch ``cuda``).
+
+    from mace_mps_kernels_b200 import patch_model
+    report = patch_model(model)          # model already on a CUDA device, float32; modified in place
+
+Replaces, where supported (same contract as Yike-Ye/mace-mps-kernels, reference src/mace_mps_kernels/__init__.py):
+  * each interaction block's convolution (gather -> channel-wise tensor product -> scatter-sum) via MACE's own
+    ``conv_fusion`` hook,
+  * each product block's symmetric contraction.
+Everything else stays on the original PyTorch path.  Inference only: the backward pass is first order (energies,
+forces, stress, relaxations, MD); double backward raises an error.
+"""
+import inspect
+import warnings
+
+import torch
+
+from .conv import CudaConvTP, MetalConvTP, conv_supported
+from .symmetric import CudaSymmetricContraction, MetalSymmetricContraction, sc_supported
+
+__version__ = '0.1.0'
+__all__ = ['patch_model', 'CudaConvTP', 'CudaSymmetricContraction', 'MetalConvTP', 'MetalSymmetricContraction']
+
+
+def _block_has_conv_fusion(blk):
+    try:
+        return 'conv_fusion' in inspect.getsource(type(blk).forward)
+    except (OSError, TypeError):
+        return False
+
+
+def patch_model(model, conv=True, symmetric=True, verbose=True):
+    """Swap supported ops for CUDA kernels, in place.  Returns {'patched': [...], 'skipped': [(name, reason)]}.
+
+    Mirrors reference ``__init__.py:34-79``: a float32 model on the accelerator (here CUDA), interaction blocks that
+    expose MACE's ``conv_fusion`` path, product blocks without the cuequivariance layout; already-patched blocks are
+    left alone (idempotent) and every skip is reported (and warned about when ``verbose``)."""
+    p0 = next(model.parameters())
+    dev = p0.device
+    if dev.type != 'cuda':
+        raise RuntimeError(f'model must be on a cuda device (found {dev})')
+    if p0.dtype != torch.float32:
+        raise RuntimeError('float32 models only')
+    patched, skipped = [], []
+    with torch.cuda.device(dev):
+        if conv:
+            for i, blk in enumerate(getattr(model, 'interactions', [])):
+                name = f'interactions.{i}.conv_tp'
+                if isinstance(getattr(blk, 'conv_tp', None), CudaConvTP):
+                    continue
+                if hasattr(blk, 'conv_fusion'):
+                    skipped.append((name, 'block already uses another fused convolution'))
+                    continue
+                if not _block_has_conv_fusion(blk):
+                    skipped.append((name, f'{type(blk).__name__} has no conv_fusion path'))
+                    continue
+                ok, why = conv_supported(blk.conv_tp)
+                if not ok:
+                    skipped.append((name, why))
+                    continue
+                blk.conv_tp = CudaConvTP(blk.conv_tp)
+                blk.conv_fusion = True
+                patched.append(name)
+        if symmetric:
+            for i, prod in enumerate(getattr(model, 'products', [])):
+                name = f'products.{i}.symmetric_contractions'
+                sc = getattr(prod, 'symmetric_contractions', None)
+                if isinstance(sc, CudaSymmetricContraction):
+                    continue
+                cfg = getattr(prod, 'cueq_config', None)
+                if cfg is not None and getattr(cfg, 'enabled', False):
+                    skipped.append((name, 'cuequivariance layout'))
+                    continue
+                ok, why = sc_supported(sc)
+                if not ok:
+                    skipped.append((name, why))
+                    continue
+                prod.symmetric_contractions = CudaSymmetricContraction(sc, device=dev)
+                patched.append(name)
+    if verbose:
+        for name, why in skipped:
+            warnings.warn(f'mace-b200-kernels: kept e3nn for {name}: {why}')
+    return dict(patched=patched, skipped=skipped)

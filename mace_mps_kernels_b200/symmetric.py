@@ -1,0 +1,203 @@
+"""MACE SymmetricContraction on B200 as a precomputed element-dependent polynomial.
+
+At inference the product-basis weights and U matrices are constants, so for element e, channel c and output
+component M the contraction is a polynomial in the channel's features x = x[b, c, :] (n_ell = (l_max+1)^2):
+    out[b, c, M] = sum_{nu} sum_{i1 <= .. <= i_nu} T_nu[e, c, M, i] x_i1 .. x_i_nu
+with T_nu = U_nu . W_nu symmetrised over index order (the reference's construction, symmetric.py:20-39; here the
+symmetrisation is one matrix product with the 0/1 map "index tuple -> sorted tuple").  Terms whose coefficient
+vanishes for every (e, M, c) are dropped (tolerance 1e-12, symmetric.py:66).  Coefficients are packed as
+T[e][row][c] (row = term's first row + M) so the channel threads of a node read consecutive addresses; terms are
+ordered by degree (descending) then index tuple, as in the reference (symmetric.py:64-69).
+
+The CUDA kernels (one thread per (node, channel), monomial list baked into NVRTC-compiled code) evaluate the
+polynomial (forward) and its derivative (first-order backward); double backward raises.
+"""
+from __future__ import annotations
+
+import itertools
+
+import numpy as np
+import torch
+
+from . import _lib
+from .conv import DOUBLE_BACKWARD_MSG, _LayerHandle
+
+
+def _contraction_tensors(ct):
+    corr = int(ct.correlation)
+    U = {nu: getattr(ct, f'U_matrix_{nu}').detach().cpu().double().numpy() for nu in range(1, corr + 1)}
+    W = {corr: ct.weights_max.detach().cpu().double().numpy()}
+    for j, w in enumerate(ct.weights):                      # weights[0] <-> nu = corr-1, weights[1] <-> corr-2, ...
+        W[corr - 1 - j] = w.detach().cpu().double().numpy()
+    has_m = U[1].ndim == 3                                   # [M, n_ell, p] for L > 0, [n_ell, p] for L = 0
+    M = U[1].shape[0] if has_m else 1
+    n_ell = U[1].shape[-2]
+    return corr, U, W, has_m, M, n_ell
+
+
+def _sym_map(n_ell, nu):
+    """(sorted index tuples in lexicographic order, 0/1 matrix [n_ell^nu, n_sym] mapping each tuple to its sort)."""
+    tuples = list(itertools.combinations_with_replacement(range(n_ell), nu))
+    pos = {t: i for i, t in enumerate(tuples)}
+    P = np.zeros((n_ell ** nu, len(tuples)))
+    for flat, idx in enumerate(itertools.product(range(n_ell), repeat=nu)):
+        P[flat, pos[tuple(sorted(idx))]] = 1.0
+    return tuples, P
+
+
+def poly_coeffs(ct):
+    """{nu: (tuples, coeffs[e, M, c, n_sym])} in float64, M = 2L+1 of this contraction's output."""
+    corr, U, W, has_m, M, n_ell = _contraction_tensors(ct)
+    res = {}
+    for nu in range(1, corr + 1):
+        u = U[nu] if has_m else U[nu][None]
+        K = u.shape[-1]
+        tuples, P = _sym_map(n_ell, nu)
+        u_sym = np.einsum('mfk,fs->msk', u.reshape(M, -1, K), P)          # [M, n_sym, K]
+        T = np.einsum('msk,ekc->emcs', u_sym, W[nu])                       # [e, M, c, n_sym]
+        res[nu] = (tuples, T)
+    return res, M, n_ell
+
+
+def sc_supported(sc):
+    try:
+        cts = list(sc.contractions)
+        for ct in cts:
+            _ = ct.correlation, ct.weights_max, ct.U_matrix_1
+    except AttributeError as e:
+        return False, f'not a MACE SymmetricContraction ({e})'
+    return True, ''
+
+
+class SCSpec:
+    def __init__(self, sc, tol=1e-12):
+        ok, why = sc_supported(sc)
+        if not ok:
+            raise ValueError(why)
+        self.blocks, rows, out_off = [], [], 0
+        self.n_ell = None
+        self.max_degree = 0
+        for ct in sc.contractions:
+            coeffs, M, n_ell = poly_coeffs(ct)
+            if self.n_ell not in (None, n_ell):
+                raise ValueError('contractions disagree on the number of feature components')
+            self.n_ell = n_ell
+            terms = []
+            for nu in sorted(coeffs, reverse=True):
+                tuples, T = coeffs[nu]
+                self.max_degree = max(self.max_degree, nu)
+                for s, idx in enumerate(tuples):
+                    v = T[..., s]                                          # [e, M, c]
+                    if np.abs(v).max() <= tol:
+                        continue
+                    terms.append((idx, len(rows)))
+                    rows += [v[:, m, :] for m in range(M)]
+            self.C = T.shape[2]
+            self.blocks.append(dict(M=M, terms=terms, out_off=out_off))
+            out_off += self.C * M
+        self.out_dim, self.nrows = out_off, len(rows)
+        self.T = torch.tensor(np.stack(rows, axis=1), dtype=torch.float32)   # [e, rows, c]
+        self.n_terms = sum(len(b['terms']) for b in self.blocks)
+
+    def descriptor(self):
+        keep = {}
+        terms = [t for b in self.blocks for t in b['terms']]
+        D = self.max_degree
+        keep['M'] = _lib.int_array(b['M'] for b in self.blocks)
+        keep['nt'] = _lib.int_array(len(b['terms']) for b in self.blocks)
+        keep['deg'] = _lib.int_array(len(idx) for idx, _ in terms)
+        keep['idx'] = _lib.int_array(v for idx, _ in terms for v in (list(idx) + [-1] * (D - len(idx))))
+        keep['row'] = _lib.int_array(r for _, r in terms)
+        d = _lib.SCDesc(self.C, self.n_ell, self.nrows, len(self.blocks), keep['M'], keep['nt'], D, keep['deg'],
+                        keep['idx'], keep['row'])
+        d._keep = keep
+        return d
+
+    def flops(self):
+        """(forward, backward) fp32 operations per (node, channel), counted from the term list."""
+        fwd = bwd = 0
+        for b in self.blocks:
+            M = b['M']
+            for idx, _ in b['terms']:
+                fwd += (len(idx) - 1) + 2 * M
+                bwd += 2 * M + len(set(idx)) * (len(idx) + 1)
+        return fwd, bwd
+
+
+_ELEM_CACHE = []
+
+
+def element_index(node_attrs: torch.Tensor):
+    """int32 argmax of the one-hot node attributes on the device (reference symmetric.py:169), cached per tensor."""
+    import weakref
+    for ref, ver, e in reversed(_ELEM_CACHE):
+        if ref() is node_attrs and ver == node_attrs._version:
+            return e
+    a = node_attrs.contiguous()
+    if a.dtype != torch.float32 or not a.is_cuda:
+        raise TypeError('node_attrs must be a float32 CUDA tensor')
+    elem = torch.empty(a.shape[0], dtype=torch.int32, device=a.device)
+    _lib.call('mmk_elem_index', _lib.ptr(a), a.shape[0], a.shape[1], _lib.ptr(elem), _lib.stream_of(a))
+    _ELEM_CACHE.append((weakref.ref(node_attrs), node_attrs._version, elem))
+    del _ELEM_CACHE[:-4]
+    return elem
+
+
+class _SCFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, elem, op):
+        if x.dtype != torch.float32 or not x.is_cuda:
+            raise TypeError(f'x must be a float32 CUDA tensor (got {x.dtype} on {x.device})')
+        x = x.contiguous()
+        N = x.shape[0]
+        if x.shape != (N, op.spec.C, op.spec.n_ell):
+            raise ValueError(f'x must be [N, {op.spec.C}, {op.spec.n_ell}] (got {tuple(x.shape)})')
+        out = torch.empty(N, op.spec.out_dim, device=x.device, dtype=torch.float32)
+        _lib.call('mmk_sc_fwd', op.handle, _lib.ptr(x), _lib.ptr(elem), _lib.ptr(op.T), _lib.ptr(out), N,
+                  _lib.stream_of(x))
+        ctx.save_for_backward(x, elem)
+        ctx.op = op
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        if torch.is_grad_enabled():          # only true under create_graph=True
+            raise RuntimeError(DOUBLE_BACKWARD_MSG)
+        x, elem = ctx.saved_tensors
+        op = ctx.op
+        g = g.contiguous()
+        gx = torch.empty_like(x)
+        _lib.call('mmk_sc_bwd', op.handle, _lib.ptr(x), _lib.ptr(elem), _lib.ptr(op.T), _lib.ptr(g), _lib.ptr(gx),
+                  x.shape[0], _lib.stream_of(x))
+        return gx, None, None
+
+
+class CudaSymmetricContraction(torch.nn.Module):
+    """Drop-in for mace ``SymmetricContraction`` at inference: forward(x[N, C, n_ell], node_attrs[N, n_elem])."""
+
+    def __init__(self, sc, device='cuda'):
+        super().__init__()
+        self.spec = SCSpec(sc)
+        self.register_buffer('T', self.spec.T.to(device).contiguous())
+        self._h = _LayerHandle('mmk_sc_layer_create', 'mmk_sc_layer_destroy', self.spec.descriptor())
+        self.irreps_in, self.irreps_out = sc.irreps_in, sc.irreps_out
+
+    @property
+    def handle(self):
+        return self._h.value
+
+    def __deepcopy__(self, memo):
+        import copy
+        new = self.__class__.__new__(self.__class__)
+        torch.nn.Module.__init__(new)
+        new.spec = self.spec
+        new.register_buffer('T', copy.deepcopy(self.T, memo))
+        new._h = self._h
+        new.irreps_in, new.irreps_out = self.irreps_in, self.irreps_out
+        return new
+
+    def forward(self, x, y):
+        return _SCFn.apply(x, element_index(y), self)
+
+
+MetalSymmetricContraction = CudaSymmetricContraction

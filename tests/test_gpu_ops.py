@@ -1,0 +1,157 @@
+"""Per-op parity of the CUDA kernels (through the C ABI) against the float64 CPU oracle.
+
+Tolerance: fp32 kernels vs fp64 oracle, max |gpu - oracle| <= REL * max |oracle| (+ a tiny absolute floor for
+all-zero outputs); the CSR builder is checked bit-exactly against a stable argsort.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import helpers
+from oracle import conv_ref, sc_ref
+
+pytestmark = pytest.mark.gpu
+
+REL = 2e-5
+
+
+def close(gpu, ref, rel=REL, what=''):
+    gpu = gpu.detach().double().cpu().numpy() if torch.is_tensor(gpu) else np.asarray(gpu)
+    ref = np.asarray(ref)
+    assert gpu.shape == ref.shape, (what, gpu.shape, ref.shape)
+    scale = max(np.abs(ref).max(initial=0.0), 1e-30)
+    err = np.abs(gpu - ref).max(initial=0.0)
+    assert err <= rel * scale + 1e-30, f'{what}: max err {err:.3e} vs scale {scale:.3e} (rel {err / scale:.2e})'
+    return err / scale
+
+
+CONV_CASES = [
+    # hidden irreps of the node features, lmax, N, E
+    ('32x0e', 3, 37, 300),
+    ('32x0e+32x1o', 3, 50, 700),
+    ('64x0e+64x1o', 2, 41, 333),
+    ('128x0e+128x1o', 3, 160, 5000),
+    ('128x0e+128x1o+128x2e', 3, 90, 2000),
+    ('96x0e+96x1o', 3, 3, 17),
+]
+
+
+@pytest.mark.parametrize('hidden,lmax,N,E', CONV_CASES)
+def test_conv_fwd_bwd_matches_oracle(cuda, hidden, lmax, N, E):
+    from mace_mps_kernels_b200.conv import CudaConvTP
+    torch.manual_seed(0)
+    tp = helpers.conv_tp(hidden, lmax).to(cuda)
+    op = CudaConvTP(tp)
+    spec, coef = conv_ref.probe_coefficients(tp)
+    ei = helpers.random_graph(N, E, seed=N, isolated=[1] if N > 3 else ())
+    x = torch.randn(N, spec['x_dim'], device=cuda)
+    Y = torch.randn(E, spec['y_dim'], device=cuda)
+    W = torch.randn(E, tp.weight_numel, device=cuda)
+    x.requires_grad_(True); Y.requires_grad_(True); W.requires_grad_(True)
+    out = op(x, Y, W, ei.to(cuda))
+    send, recv = ei[0].numpy(), ei[1].numpy()
+    ref = conv_ref.conv_fwd(spec, coef, x.detach().cpu(), Y.detach().cpu(), W.detach().cpu(), send, recv, N)
+    close(out, ref, what='out')
+    g = torch.randn_like(out)
+    gx, gY, gW = torch.autograd.grad(out, (x, Y, W), g)
+    rgx, rgY, rgW = conv_ref.conv_bwd(spec, coef, x.detach().cpu(), Y.detach().cpu(), W.detach().cpu(), g.cpu(),
+                                      send, recv)
+    close(gx, rgx, what='gx')
+    close(gY, rgY, what='gY')
+    close(gW, rgW, what='gW')
+    # the unpatched e3nn-style path on the GPU (fp32) agrees too
+    mji = tp(x.detach()[ei[0].to(cuda)], Y.detach(), W.detach())
+    msg = torch.zeros_like(out).index_add_(0, ei[1].to(cuda), mji)
+    close(out, msg.double().cpu().numpy(), rel=1e-4, what='vs torch path')
+
+
+def test_conv_no_edges_and_isolated_nodes(cuda):
+    from mace_mps_kernels_b200.conv import CudaConvTP
+    tp = helpers.conv_tp('32x0e+32x1o', 3).to(cuda)
+    op = CudaConvTP(tp)
+    N = 5
+    x = torch.randn(N, 128, device=cuda, requires_grad=True)
+    Y = torch.randn(0, 16, device=cuda, requires_grad=True)
+    W = torch.randn(0, tp.weight_numel, device=cuda, requires_grad=True)
+    ei = torch.zeros(2, 0, dtype=torch.long, device=cuda)
+    out = op(x, Y, W, ei)
+    assert out.shape == (N, 32 * 40) and float(out.abs().max()) == 0.0
+    gx, = torch.autograd.grad(out, (x,), torch.randn_like(out))
+    assert float(gx.abs().max()) == 0.0
+
+
+@pytest.mark.parametrize('N,E,seed', [(1, 0, 0), (7, 50, 1), (1000, 40000, 2), (300, 2, 3)])
+def test_csr_matches_stable_argsort(cuda, N, E, seed):
+    from mace_mps_kernels_b200.conv import csr_build
+    rng = np.random.default_rng(seed)
+    idx = rng.integers(0, N, E) if seed != 2 else np.repeat(np.arange(N), E // N)[rng.permutation(E)]
+    rowptr, eids = csr_build(torch.from_numpy(idx).to(cuda), N)
+    r0, e0 = conv_ref.csr_by(idx, N)
+    assert np.array_equal(rowptr.cpu().numpy(), r0)
+    assert np.array_equal(eids.cpu().numpy(), e0)
+
+
+def test_csr_flags_out_of_range(cuda):
+    from mace_mps_kernels_b200 import _lib
+    idx = torch.tensor([0, 5, 1, -1, 2], device=cuda)
+    N = 3
+    rowptr = torch.empty(N + 1, dtype=torch.int32, device=cuda)
+    eids = torch.empty(5, dtype=torch.int32, device=cuda)
+    flag = torch.zeros(1, dtype=torch.int32, device=cuda)
+    nb = _lib.lib().mmk_csr_workspace_bytes(N, 5)
+    ws = torch.empty(nb, dtype=torch.uint8, device=cuda)
+    _lib.call('mmk_csr_build', _lib.ptr(idx), 5, N, _lib.ptr(rowptr), _lib.ptr(eids), _lib.ptr(ws), nb, _lib.ptr(flag),
+              _lib.stream_of(idx))
+    assert int(flag.item()) == 1
+    assert rowptr.cpu().tolist() == [0, 1, 2, 3]
+    assert eids[:3].cpu().tolist() == [0, 2, 4]
+
+
+SC_CASES = [
+    ('32x0e+32x1o', 3, 3, 40),
+    ('128x0e+128x1o', 3, 3, 160),
+    ('128x0e', 3, 3, 33),
+    ('64x0e', 2, 2, 20),
+    ('32x0e+32x1o+32x2e', 3, 3, 25),
+]
+
+
+@pytest.mark.parametrize('hidden,lmax,corr,N', SC_CASES)
+def test_sc_fwd_bwd_matches_oracle(cuda, hidden, lmax, corr, N):
+    from mace_mps_kernels_b200.standin import o3
+    from mace_mps_kernels_b200.standin.symmetric_contraction import SymmetricContraction
+    from mace_mps_kernels_b200.symmetric import CudaSymmetricContraction
+    torch.manual_seed(1)
+    hid = o3.Irreps(hidden)
+    C = hid[0].mul
+    sh = o3.Irreps.spherical_harmonics(lmax)
+    n_elem = 4
+    sc = SymmetricContraction((sh * C).sort()[0].simplify(), hid, corr, n_elem).to(cuda)
+    op = CudaSymmetricContraction(sc, device=cuda)
+    spec = sc_ref.sc_spec(sc)
+    x = torch.randn(N, C, (lmax + 1) ** 2, device=cuda, requires_grad=True)
+    elem = torch.randint(0, n_elem, (N,))
+    attrs = torch.nn.functional.one_hot(elem, n_elem).float().to(cuda)
+    out = op(x, attrs)
+    ref = sc_ref.sc_fwd(spec, x.detach().cpu(), elem.numpy())
+    close(out, ref, what='sc out')
+    close(out, sc(x.detach(), attrs).double().cpu().numpy(), rel=1e-4, what='sc vs torch path')
+    g = torch.randn_like(out)
+    gx, = torch.autograd.grad(out, (x,), g)
+    close(gx, sc_ref.sc_bwd(spec, x.detach().cpu(), elem.numpy(), g.cpu()), what='sc gx')
+
+
+def test_double_backward_raises_on_ops(cuda):
+    from mace_mps_kernels_b200.conv import CudaConvTP
+    tp = helpers.conv_tp('32x0e+32x1o', 3).to(cuda)
+    op = CudaConvTP(tp)
+    ei = helpers.random_graph(6, 20).to(cuda)
+    x = torch.randn(6, 128, device=cuda, requires_grad=True)
+    Y = torch.randn(20, 16, device=cuda)
+    W = torch.randn(20, tp.weight_numel, device=cuda)
+    out = op(x, Y, W, ei)
+    with pytest.raises(RuntimeError, match='double backward'):
+        (g,) = torch.autograd.grad(out.square().sum(), x, create_graph=True)
+        torch.autograd.grad(g.sum(), x)
