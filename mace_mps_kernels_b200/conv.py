@@ -26,6 +26,11 @@ DOUBLE_BACKWARD_MSG = ('mace-b200-kernels: double backward (create_graph=True, e
                        'autograd Hessian) is not supported by the CUDA kernels; use the unpatched e3nn model for that')
 
 
+class _Ir:
+    def __init__(self, l):
+        self.l = int(l)
+
+
 def _blocks(irreps):
     res, off = [], 0
     for mul, ir in irreps:
@@ -107,6 +112,27 @@ class ConvSpec:
                 if abs(v) > tol:
                     c['terms'].append((a, b, m, v))
         self.nnz = sum(len(c['terms']) for c in self.coef)
+
+    @classmethod
+    def from_table(cls, mul, in1_l, in2_l, out_l, ins, terms):
+        """Spec from an explicit coefficient table: ``ins`` = [(i_in1, i_in2, i_out)], ``terms`` = [(k, a, b, m, c)]."""
+        self = cls.__new__(cls)
+        mk = lambda ls, mult: _blocks([(mult, _Ir(l)) for l in ls])
+        self.in1, self.x_dim = mk(in1_l, mul)
+        self.in2, self.y_dim = mk(in2_l, 1)
+        self.outb, self.out_dim = mk(out_l, mul)
+        self.mul = mul
+        self.ins = [tuple(int(v) for v in t) for t in ins]
+        self.nins = len(self.ins)
+        self.w_dim = self.nins * mul
+        self.coef = []
+        for k, (i1, i2, io) in enumerate(self.ins):
+            self.coef.append(dict(k=k, l1=self.in1[i1][0], l2=self.in2[i2][0], l3=self.outb[io][0], o1=self.in1[i1][2],
+                                  o2=self.in2[i2][2], o3=self.outb[io][2], terms=[]))
+        for k, a, b, m, c in terms:
+            self.coef[int(k)]['terms'].append((int(a), int(b), int(m), float(c)))
+        self.nnz = len(terms)
+        return self
 
     def descriptor(self):
         """ctypes ``mmk_conv_desc`` (arrays kept alive on the returned object)."""
@@ -233,12 +259,21 @@ class CudaConvTP(torch.nn.Module):
     """Replacement for an interaction block's ``conv_tp`` under MACE's ``conv_fusion`` path:
     forward(node_feats, edge_attrs, tp_weights, edge_index) -> summed messages [N, OUT_DIM]."""
 
-    def __init__(self, tp):
+    def __init__(self, tp, spec=None):
         super().__init__()
-        self.spec = ConvSpec(tp)
+        self.spec = ConvSpec(tp) if spec is None else spec
         self._h = _LayerHandle('mmk_conv_layer_create', 'mmk_conv_layer_destroy', self.spec.descriptor())
-        self.irreps_in1, self.irreps_in2, self.irreps_out = tp.irreps_in1, tp.irreps_in2, tp.irreps_out
-        self.weight_numel = tp.weight_numel
+        if tp is not None:
+            self.irreps_in1, self.irreps_in2, self.irreps_out = tp.irreps_in1, tp.irreps_in2, tp.irreps_out
+            self.weight_numel = tp.weight_numel
+        else:
+            self.irreps_in1 = self.irreps_in2 = self.irreps_out = None
+            self.weight_numel = self.spec.w_dim
+
+    @classmethod
+    def from_spec(cls, spec):
+        """Op for an explicit ``ConvSpec`` (e.g. ``ConvSpec.from_table``) without a TensorProduct object."""
+        return cls(None, spec)
 
     @property
     def handle(self):

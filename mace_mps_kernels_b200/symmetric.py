@@ -99,6 +99,23 @@ class SCSpec:
         self.T = torch.tensor(np.stack(rows, axis=1), dtype=torch.float32)   # [e, rows, c]
         self.n_terms = sum(len(b['terms']) for b in self.blocks)
 
+    @classmethod
+    def from_table(cls, C, n_ell, block_M, block_terms, T):
+        """Spec from an explicit table: block_terms[q] = [(index tuple, first row)], T [n_elem, rows, C]."""
+        self = cls.__new__(cls)
+        self.C, self.n_ell = int(C), int(n_ell)
+        self.blocks, out_off = [], 0
+        for M, terms in zip(block_M, block_terms):
+            self.blocks.append(dict(M=int(M), terms=[(tuple(int(i) for i in idx), int(r)) for idx, r in terms],
+                                    out_off=out_off))
+            out_off += self.C * int(M)
+        self.out_dim = out_off
+        self.T = torch.as_tensor(np.asarray(T), dtype=torch.float32)
+        self.nrows = self.T.shape[1]
+        self.n_terms = sum(len(b['terms']) for b in self.blocks)
+        self.max_degree = max(len(idx) for b in self.blocks for idx, _ in b['terms'])
+        return self
+
     def descriptor(self):
         keep = {}
         terms = [t for b in self.blocks for t in b['terms']]
@@ -175,12 +192,18 @@ class _SCFn(torch.autograd.Function):
 class CudaSymmetricContraction(torch.nn.Module):
     """Drop-in for mace ``SymmetricContraction`` at inference: forward(x[N, C, n_ell], node_attrs[N, n_elem])."""
 
-    def __init__(self, sc, device='cuda'):
+    def __init__(self, sc, device='cuda', spec=None):
         super().__init__()
-        self.spec = SCSpec(sc)
+        self.spec = SCSpec(sc) if spec is None else spec
         self.register_buffer('T', self.spec.T.to(device).contiguous())
         self._h = _LayerHandle('mmk_sc_layer_create', 'mmk_sc_layer_destroy', self.spec.descriptor())
-        self.irreps_in, self.irreps_out = sc.irreps_in, sc.irreps_out
+        self.irreps_in = getattr(sc, 'irreps_in', None)
+        self.irreps_out = getattr(sc, 'irreps_out', None)
+
+    @classmethod
+    def from_spec(cls, spec, device='cuda'):
+        """Op for an explicit ``SCSpec`` (e.g. ``SCSpec.from_table``)."""
+        return cls(None, device, spec)
 
     @property
     def handle(self):
