@@ -35,6 +35,7 @@ sys.path.insert(0, ROOT)
 
 from mace_mps_kernels_b200 import _lib, patch_model, standin  # noqa: E402
 from mace_mps_kernels_b200.conv import CudaConvTP  # noqa: E402
+from mace_mps_kernels_b200.graphs import GraphedEnergyForces  # noqa: E402
 from mace_mps_kernels_b200.symmetric import CudaSymmetricContraction  # noqa: E402
 
 METRIC = 'E+F atom-steps/s'
@@ -80,7 +81,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
-                                          '-lms', '200', '-i', str(self.index)], stdout=subprocess.PIPE,
+                                          '-lms', '50', '-i', str(self.index)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -149,50 +150,63 @@ def conv_bytes(spec, N, E):
 
 
 def time_ops(calls, reps, flush):
-    """CUDA-event time per launch of every patched op's forward and backward kernel (L2 flushed before each)."""
+    """CUDA-event time of each patched op's forward and backward kernel, launched directly through the C ABI with
+    preallocated outputs; a 256 MB L2 flush is enqueued before every launch, which also hides the host launch."""
+    from mace_mps_kernels_b200.conv import graph_csr
     res = []
     stream = torch.cuda.current_stream()
+    st = _lib.stream_of(torch.empty(1, device='cuda'))
+    P = _lib.ptr
+    n_conv = n_sc = 0
     for mod, args, out in calls:
         if isinstance(mod, CudaConvTP):
-            x, Y, W, ei = args
-            x, Y, W = x.clone().requires_grad_(True), Y.clone().requires_grad_(True), W.clone().requires_grad_(True)
-            kind = 'conv'
+            x, Y, W, ei = (a.contiguous() for a in args)
+            N, E = x.shape[0], Y.shape[0]
+            rr, re_, sr, se = graph_csr(ei, N)
+            o = torch.empty_like(out)
+            g = torch.randn_like(out)
+            gx, gY, gW = torch.empty_like(x), torch.empty_like(Y), torch.empty_like(W)
+            recv = ei.data_ptr() + E * 8
+            fwd = lambda: _lib.call('mmk_conv_fwd', mod.handle, P(x), P(Y), P(W), P(rr), P(re_), P(ei), P(o), N, E, st)
+            bwd = lambda: _lib.call('mmk_conv_bwd', mod.handle, P(x), P(Y), P(W), P(g), P(sr), P(se), recv, P(gx),
+                                    P(gY), P(gW), N, E, st)
+            kind, name = 'conv', f'conv_tp[{n_conv}]'
+            n_conv += 1
         else:
-            x, attrs = args
-            x = x.clone().requires_grad_(True)
-            kind = 'sc'
-        g = torch.randn_like(out)
-        tf, tb = [], []
-        for r in range(reps + 2):
-            flush(stream)
-            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-            e0.record()
-            o = mod(x, Y, W, ei) if kind == 'conv' else mod(x, attrs)
-            e1.record()
-            flush(stream)
-            e1b = torch.cuda.Event(enable_timing=True)
-            e1b.record()
-            torch.autograd.backward(o, g)
-            e2.record()
-            torch.cuda.synchronize()
-            if r >= 2:
-                tf.append(e0.elapsed_time(e1))
-                tb.append(e1b.elapsed_time(e2))
-            x.grad = None
-            if kind == 'conv':
-                Y.grad = W.grad = None
-        N = x.shape[0]
+            from mace_mps_kernels_b200.symmetric import element_index
+            x, attrs = (a.contiguous() for a in args)
+            N = x.shape[0]
+            elem = element_index(attrs)
+            o = torch.empty_like(out)
+            g = torch.randn_like(out)
+            gx = torch.empty_like(x)
+            fwd = lambda: _lib.call('mmk_sc_fwd', mod.handle, P(x), P(elem), P(mod.T), P(o), N, st)
+            bwd = lambda: _lib.call('mmk_sc_bwd', mod.handle, P(x), P(elem), P(mod.T), P(g), P(gx), N, st)
+            kind, name = 'sc', f'symcon[{n_sc}]'
+            n_sc += 1
+        times = {}
+        for tag, fn in (('fwd', fwd), ('bwd', bwd)):
+            ts = []
+            for r in range(reps + 2):
+                flush(stream)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                e1.synchronize()
+                if r >= 2:
+                    ts.append(e0.elapsed_time(e1) * 1e3)
+            times[tag] = float(np.median(ts))
         if kind == 'conv':
-            E = Y.shape[0]
             bf, bb = conv_bytes(mod.spec, N, E)
-            res.append(dict(op=f'conv_tp L={mod.spec.x_dim // mod.spec.mul}', kind=kind, N=N, E=E,
-                            fwd_us=1e3 * float(np.mean(tf)), bwd_us=1e3 * float(np.mean(tb)), fwd_bytes=bf,
-                            bwd_bytes=bb))
+            res.append(dict(op=name, kind=kind, N=N, E=E, nnz=mod.spec.nnz, fwd_us=times['fwd'],
+                            bwd_us=times['bwd'], fwd_bytes=bf, bwd_bytes=bb,
+                            fwd_gbs=bf / times['fwd'] * 1e-3, bwd_gbs=bb / times['bwd'] * 1e-3))
         else:
             ff, fb = mod.spec.flops()
             C = mod.spec.C
-            res.append(dict(op=f'symcon out_dim={mod.spec.out_dim}', kind=kind, N=N, fwd_us=1e3 * float(np.mean(tf)),
-                            bwd_us=1e3 * float(np.mean(tb)), fwd_flops=ff * N * C, bwd_flops=fb * N * C))
+            res.append(dict(op=name, kind=kind, N=N, terms=mod.spec.n_terms, fwd_us=times['fwd'],
+                            bwd_us=times['bwd'], fwd_flops=ff * N * C, bwd_flops=fb * N * C))
     return res
 
 
@@ -218,7 +232,7 @@ def cpu_baseline(n_steps_cap=5, budget_s=20.0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--steps', type=int, default=300)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--op-reps', type=int, default=10)
@@ -251,14 +265,25 @@ def main():
     flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     e_all = torch.zeros(world, device=dev)
 
-    def step(b):
-        E, F = e_and_f(model, b)
+    # eager E+F (for reference in the JSON line), then the CUDA-graphed E+F that is timed
+    for _ in range(a.warmup):
+        e_and_f(model, batch)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(5):
+        e_and_f(model, batch)
+    torch.cuda.synchronize()
+    eager_ms = (time.perf_counter() - t0) / 5 * 1e3
+    graphed = GraphedEnergyForces(model, batch)
+
+    def step(b=None):
+        E, F = graphed(b)
         if dist is not None:
-            dist.all_gather_into_tensor(e_all, E.detach().reshape(1))
+            dist.all_gather_into_tensor(e_all, E.reshape(1))
         return E, F
 
     for _ in range(a.warmup):
-        step(batch)
+        step()
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
@@ -274,13 +299,13 @@ def main():
             flush_l2(flush_buf)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            step(batch)
+            step()
             e1.record()
             evs.append((e0, e1))
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
-    launches = sum(_lib.LAUNCHES.values())
+    launches = graphed.kernels_per_replay * a.steps
     ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / a.steps
     ms_t = torch.tensor([ms], device=dev)
     if dist is not None:
@@ -301,7 +326,7 @@ def main():
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         b = {k: (v.to(dev, non_blocking=True) if torch.is_tensor(v) else v) for k, v in pinned.items()}
-        E, F = step(b)
+        E, F = step(b)                       # copies into the captured graph's static inputs, replays
         forces_host.copy_(F, non_blocking=True)
         e_host = E.detach().to('cpu', non_blocking=True)
         e1.record()
@@ -343,6 +368,7 @@ def main():
             'e2e': {'value': round(n_atoms * world / (ms_e2e * 1e-3), 1), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
                     'd2h_bytes_per_step': d2h, 'ms_per_step': round(ms_e2e, 4)},
             'roofline': roofline, 'cpu_baseline': cpu, 'gpu_launches': launches, 'clocks': clk.summary(),
+            'eager_ms_per_step': round(eager_ms, 3),
             'ops': [{k: (round(v, 2) if isinstance(v, float) else v) for k, v in o.items()} for o in ops],
         }
         print(json.dumps(res))

@@ -83,7 +83,7 @@ def energy_forces(model, structure, device, R=None):
     st = structure if R is None else structure.rotated(R)
     b = batch_for([st], device)
     out = model(b, compute_force=True, training=False)
-    return float(out['energy'].sum()), out['forces'].detach().cpu().double().numpy()
+    return float(out['energy'].detach().sum()), out['forces'].detach().cpu().double().numpy()
 
 
 def pair(config, device):

@@ -62,8 +62,9 @@ def test_conv_fwd_bwd_matches_oracle(cuda, hidden, lmax, N, E):
     close(gY, rgY, what='gY')
     close(gW, rgW, what='gW')
     # the unpatched e3nn-style path on the GPU (fp32) agrees too
-    mji = tp(x.detach()[ei[0].to(cuda)], Y.detach(), W.detach())
-    msg = torch.zeros_like(out).index_add_(0, ei[1].to(cuda), mji)
+    with torch.no_grad():
+        mji = tp(x.detach()[ei[0].to(cuda)], Y.detach(), W.detach())
+        msg = torch.zeros_like(out).index_add_(0, ei[1].to(cuda), mji)
     close(out, msg.double().cpu().numpy(), rel=1e-4, what='vs torch path')
 
 
@@ -137,7 +138,8 @@ def test_sc_fwd_bwd_matches_oracle(cuda, hidden, lmax, corr, N):
     out = op(x, attrs)
     ref = sc_ref.sc_fwd(spec, x.detach().cpu(), elem.numpy())
     close(out, ref, what='sc out')
-    close(out, sc(x.detach(), attrs).double().cpu().numpy(), rel=1e-4, what='sc vs torch path')
+    with torch.no_grad():
+        close(out, sc(x.detach(), attrs).double().cpu().numpy(), rel=1e-4, what='sc vs torch path')
     g = torch.randn_like(out)
     gx, = torch.autograd.grad(out, (x,), g)
     close(gx, sc_ref.sc_bwd(spec, x.detach().cpu(), elem.numpy(), g.cpu()), what='sc gx')
