@@ -36,6 +36,26 @@ class Structure:
     def rotated(self, R):
         return Structure(self.positions @ R.T, self.numbers.copy(), self.cell @ R.T, self.pbc.copy())
 
+    def permuted(self, perm):
+        perm = np.asarray(perm)
+        return Structure(self.positions[perm].copy(), self.numbers[perm].copy(), self.cell.copy(), self.pbc.copy())
+
+
+def morton_order(positions, cell, bits=10):
+    """Permutation sorting atoms along a Z-order (Morton) curve of their fractional coordinates.
+
+    Atoms close in space get close indices, so the rows a block of receivers gathers from its neighbours overlap
+    and stay in L2 while the convolution streams the per-edge weights."""
+    f = np.asarray(positions, np.float64) @ np.linalg.inv(np.asarray(cell, np.float64))
+    f = f - np.floor(f.min(0))
+    f = f / max(f.max(), 1e-12)
+    q = np.minimum((f * (1 << bits)).astype(np.int64), (1 << bits) - 1)
+    code = np.zeros(len(q), np.int64)
+    for b in range(bits):
+        for ax in range(3):
+            code |= ((q[:, ax] >> b) & 1) << (3 * b + ax)
+    return np.argsort(code, kind='stable')
+
 
 def fcc100_slab(symbol, a, nx, ny, nlayers, vacuum):
     """Square (100) surface cells of side a/sqrt2; layer k at z = k a/2, odd layers shifted by half a cell."""

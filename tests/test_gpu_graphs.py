@@ -22,6 +22,7 @@ def test_graphed_matches_eager(cuda):
     b0 = batches[0]
     g = GraphedEnergyForces(met, b0)
     E, F = g(b0)
+    E, F = E.clone(), F.clone()          # the graph's outputs are static buffers, overwritten by the next call
     out = met(dict(b0))
     assert abs(float(E.sum()) - float(out['energy'].detach().sum())) < 1e-4
     assert float((F - out['forces']).abs().max()) < 1e-5
