@@ -112,6 +112,22 @@ MMK_API size_t mmk_csr_workspace_bytes(int64_t n_nodes, int64_t n_edges);
 MMK_API int mmk_csr_build(const int64_t *index, int64_t n_edges, int64_t n_nodes, int32_t *rowptr, int32_t *eids,
                   void *workspace, size_t workspace_bytes, int32_t *error_flag, void *stream);
 
+/* Same result as mmk_csr_build, for callers that cannot allocate device memory: an MD engine or plugin host that
+ * owns every device allocation through its own pool and hands this library only its inputs and outputs, or code
+ * that must not call cudaMalloc where it runs.  This entry point has no counterpart in the reference (which always
+ * lets PyTorch allocate); it allocates nothing.  Its scratch is one array of fixed size inside this library's
+ * device image, so every GPU that loads the library holds it until the process exits:
+ *   n_nodes <= MMK_NOALLOC_MAX_NODES and n_edges <= MMK_NOALLOC_MAX_EDGES (17 MiB per GPU); larger inputs return
+ *   MMK_ERR_INVALID without launching anything.
+ * The first call on a device looks up that device's copy of the array (cudaGetSymbolAddress); make it before any
+ * stream capture.  All calls share the one array: calls that overlap on the GPU (different streams, or threads)
+ * race and must be serialised by the caller.  The array keeps the last call's contents; everything a call reads
+ * from it is written first by the same call. */
+#define MMK_NOALLOC_MAX_NODES (1 << 18)
+#define MMK_NOALLOC_MAX_EDGES (1 << 22)
+MMK_API int mmk_csr_build_noalloc(const int64_t *index, int64_t n_edges, int64_t n_nodes, int32_t *rowptr,
+                                  int32_t *eids, int32_t *error_flag, void *stream);
+
 /* ------------------------------------------------------------------------------------------------------------------
  * symmetric contraction layer
  * ---------------------------------------------------------------------------------------------------------------- */
