@@ -173,15 +173,16 @@ def time_ops(calls, reps, flush):
             kind, name = 'conv', f'conv_tp[{n_conv}]'
             n_conv += 1
         else:
-            from mace_mps_kernels_b200.symmetric import element_index
+            from mace_mps_kernels_b200.symmetric import element_groups
             x, attrs = (a.contiguous() for a in args)
             N = x.shape[0]
-            elem = element_index(attrs)
+            _, erow, perm = element_groups(attrs)
+            ne = erow.shape[0] - 1
             o = torch.empty_like(out)
             g = torch.randn_like(out)
             gx = torch.empty_like(x)
-            fwd = lambda: _lib.call('mmk_sc_fwd', mod.handle, P(x), P(elem), P(mod.T), P(o), N, st)
-            bwd = lambda: _lib.call('mmk_sc_bwd', mod.handle, P(x), P(elem), P(mod.T), P(g), P(gx), N, st)
+            fwd = lambda: _lib.call('mmk_sc_fwd', mod.handle, P(x), P(perm), P(erow), ne, P(mod.T), P(o), N, st)
+            bwd = lambda: _lib.call('mmk_sc_bwd', mod.handle, P(x), P(perm), P(erow), ne, P(mod.T), P(g), P(gx), N, st)
             kind, name = 'sc', f'symcon[{n_sc}]'
             n_sc += 1
         times = {}

@@ -82,6 +82,9 @@ MMK_API int mmk_conv_layer_destroy(mmk_conv_layer *layer);
 MMK_API int mmk_conv_layer_dims(const mmk_conv_layer *layer, int *x_dim, int *y_dim, int *out_dim, int *w_dim);
 /* NVRTC-compile the generated source without loading it (needs no GPU); for build checks and tests. */
 MMK_API int mmk_conv_compile_check(const mmk_conv_desc *desc);
+/* Error status of the layer's kernels on the current device (0 = ok; nonzero = a pipeline wait gave up and the kernel
+ * returned early, its outputs are invalid).  Synchronises with the device; reset != 0 clears it. */
+MMK_API int mmk_conv_layer_status(const mmk_conv_layer *layer, int32_t *status, int reset);
 
 /* Forward: out[n] = sum over the receiver-CSR segment of n.  Deterministic (fixed edge order), no atomics.
  * Replaces reference conv.py:109-141 (``conv_fwd`` kernel) as launched by conv.py:325-326.
@@ -159,15 +162,23 @@ MMK_API int mmk_sc_layer_destroy(mmk_sc_layer *layer);
 MMK_API int mmk_sc_layer_dims(const mmk_sc_layer *layer, int *C, int *n_ell, int *out_dim, int *n_rows);
 MMK_API int mmk_sc_compile_check(const mmk_sc_desc *desc);
 
+MMK_API int mmk_sc_layer_status(const mmk_sc_layer *layer, int32_t *status, int reset);
+
 /* elem[b] = argmax_e node_attrs[b, e] (first maximum), as torch.argmax (reference symmetric.py:169). */
 MMK_API int mmk_elem_index(const float *node_attrs, int64_t n_nodes, int n_elem, int32_t *elem, void *stream);
+/* Nodes grouped by element: perm[erow[e]:erow[e+1]] = the nodes of element e in increasing order (the CSR of elem;
+ * workspace: mmk_csr_workspace_bytes(n_elem, n_nodes) bytes).  The symmetric-contraction kernels work on these
+ * groups so that one coefficient row feeds several nodes. */
+MMK_API int mmk_elem_groups(const int32_t *elem, int64_t n_nodes, int n_elem, int32_t *erow, int32_t *perm,
+                            void *workspace, size_t workspace_bytes, void *stream);
 
-/* out[N, out_dim] from x[N, C, n_ell]; replaces reference symmetric.py:82-105 (``sc_fwd``). */
-MMK_API int mmk_sc_fwd(const mmk_sc_layer *layer, const float *x, const int32_t *elem, const float *T, float *out,
-               int64_t n_nodes, void *stream);
-/* gx[N, C, n_ell] = d(sum out*grad_out)/dx; replaces reference symmetric.py:106-131 (``sc_bwd``). */
-MMK_API int mmk_sc_bwd(const mmk_sc_layer *layer, const float *x, const int32_t *elem, const float *T,
-               const float *grad_out, float *gx, int64_t n_nodes, void *stream);
+/* out[N, out_dim] from x[N, C, n_ell]; replaces reference symmetric.py:82-105 (``sc_fwd``, launched at :140).
+ * perm / erow: mmk_elem_groups of the element index. */
+MMK_API int mmk_sc_fwd(const mmk_sc_layer *layer, const float *x, const int32_t *perm, const int32_t *erow, int n_elem,
+                       const float *T, float *out, int64_t n_nodes, void *stream);
+/* gx[N, C, n_ell] = d(sum out*grad_out)/dx; replaces reference symmetric.py:106-131 (``sc_bwd``, launched at :154). */
+MMK_API int mmk_sc_bwd(const mmk_sc_layer *layer, const float *x, const int32_t *perm, const int32_t *erow, int n_elem,
+                       const float *T, const float *grad_out, float *gx, int64_t n_nodes, void *stream);
 
 #ifdef __cplusplus
 }

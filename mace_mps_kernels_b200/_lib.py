@@ -40,6 +40,7 @@ SIGNATURES = {
     'mmk_conv_layer_destroy': (_i, [_p]),
     'mmk_conv_layer_dims': (_i, [_p, _ip, _ip, _ip, _ip]),
     'mmk_conv_compile_check': (_i, [ctypes.POINTER(ConvDesc)]),
+    'mmk_conv_layer_status': (_i, [_p, _ip, _i]),
     'mmk_conv_fwd': (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p]),
     'mmk_conv_bwd': (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p]),
     'mmk_csr_workspace_bytes': (_sz, [_i64, _i64]),
@@ -49,9 +50,11 @@ SIGNATURES = {
     'mmk_sc_layer_destroy': (_i, [_p]),
     'mmk_sc_layer_dims': (_i, [_p, _ip, _ip, _ip, _ip]),
     'mmk_sc_compile_check': (_i, [ctypes.POINTER(SCDesc)]),
+    'mmk_sc_layer_status': (_i, [_p, _ip, _i]),
     'mmk_elem_index': (_i, [_p, _i64, _i, _p, _p]),
-    'mmk_sc_fwd': (_i, [_p, _p, _p, _p, _p, _i64, _p]),
-    'mmk_sc_bwd': (_i, [_p, _p, _p, _p, _p, _p, _i64, _p]),
+    'mmk_elem_groups': (_i, [_p, _i64, _i, _p, _p, _p, _sz, _p]),
+    'mmk_sc_fwd': (_i, [_p, _p, _p, _p, _i, _p, _p, _i64, _p]),
+    'mmk_sc_bwd': (_i, [_p, _p, _p, _p, _i, _p, _p, _p, _i64, _p]),
 }
 
 _lib = None
@@ -85,7 +88,7 @@ def check(code):
 
 # kernels each entry point launches (bench.py reports the count issued inside its timed region)
 KERNELS_PER_CALL = {'mmk_conv_fwd': 1, 'mmk_conv_bwd': 1, 'mmk_sc_fwd': 1, 'mmk_sc_bwd': 1, 'mmk_csr_build': 4,
-                    'mmk_csr_build_noalloc': 4, 'mmk_elem_index': 1}
+                    'mmk_csr_build_noalloc': 4, 'mmk_elem_index': 1, 'mmk_elem_groups': 4}
 LAUNCHES = collections.Counter()
 
 
@@ -102,6 +105,11 @@ def stream_of(t: torch.Tensor):
 
 def ptr(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def aligned(t, nbytes=16):
+    """``t`` if its data starts on an ``nbytes`` boundary (the TMA copies need 16), else a contiguous copy."""
+    return t if t.data_ptr() % nbytes == 0 else t.clone(memory_format=torch.contiguous_format)
 
 
 def int_array(vals):

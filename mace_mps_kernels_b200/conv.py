@@ -9,8 +9,9 @@ over receivers (unnormalised; MACE divides by avg_num_neighbors afterwards).
   TensorProduct applies it) by probing the TensorProduct with unit inputs on channel 0, keeping |c| > 1e-7 -- the
   reference's method (conv.py:136-167); here all instructions are probed in one batch.
 * The kernels are generated per layer by the C library (coefficients baked in as constants, NVRTC, sm_100a):
-  forward over the receiver CSR (deterministic, no atomics); backward in one fused pass over the sender CSR giving
-  gx per sender and gW, gY per edge.
+  persistent, warp-specialised, with the per-edge rows streamed into shared memory by TMA; forward over the receiver
+  CSR (deterministic, no atomics); backward in one fused pass over the sender CSR giving gx per sender and gW, gY per
+  edge.
 * The receiver and sender CSRs are built on the GPU once per edge_index tensor (both interaction layers and the
   backward reuse them); the reference re-sorts on every forward and backward (conv.py:324, 341).
 """
@@ -206,7 +207,7 @@ class _ConvFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, Y, W, edge_index, op):
         _check_inputs(x, Y, W, edge_index, op.spec)
-        x, Y, W = x.contiguous(), Y.contiguous(), W.contiguous()
+        x, Y, W = (_lib.aligned(t.contiguous()) for t in (x, Y, W))
         ei = edge_index.to(device=x.device, dtype=torch.int64).contiguous()
         n, E = x.shape[0], Y.shape[0]
         rrow, reid, srow, seid = graph_csr(ei, n)
@@ -223,7 +224,7 @@ class _ConvFn(torch.autograd.Function):
             raise RuntimeError(DOUBLE_BACKWARD_MSG)
         x, Y, W, ei, srow, seid = ctx.saved_tensors
         op = ctx.op
-        g = g.contiguous()
+        g = _lib.aligned(g.contiguous())
         n, E = x.shape[0], Y.shape[0]
         gx = torch.empty_like(x) if ctx.needs_input_grad[0] else None
         gY = gW = None
@@ -278,6 +279,13 @@ class CudaConvTP(torch.nn.Module):
     @property
     def handle(self):
         return self._h.value
+
+    def status(self, reset=False):
+        """Error status of this layer's kernels on the current device (0 = ok); synchronises with the device."""
+        import ctypes
+        v = ctypes.c_int(0)
+        _lib.call('mmk_conv_layer_status', self.handle, ctypes.byref(v), int(reset))
+        return v.value
 
     def __deepcopy__(self, memo):
         new = self.__class__.__new__(self.__class__)

@@ -9,8 +9,9 @@ vanishes for every (e, M, c) are dropped (tolerance 1e-12, symmetric.py:66).  Co
 T[e][row][c] (row = term's first row + M) so the channel threads of a node read consecutive addresses; terms are
 ordered by degree (descending) then index tuple, as in the reference (symmetric.py:64-69).
 
-The CUDA kernels (one thread per (node, channel), monomial list baked into NVRTC-compiled code) evaluate the
-polynomial (forward) and its derivative (first-order backward); double backward raises.
+The CUDA kernels (monomial list baked into NVRTC-compiled code) evaluate the polynomial (forward) and its derivative
+(first-order backward) on tiles of nodes of one element, each coefficient row staged once in shared memory by TMA and
+applied to several nodes; double backward raises.
 """
 from __future__ import annotations
 
@@ -144,35 +145,47 @@ class SCSpec:
 _ELEM_CACHE = []
 
 
-def element_index(node_attrs: torch.Tensor):
-    """int32 argmax of the one-hot node attributes on the device (reference symmetric.py:169), cached per tensor."""
+def element_groups(node_attrs: torch.Tensor):
+    """(elem int32[N], erow int32[n_elem+1], perm int32[N]): the argmax element of every node (reference
+    symmetric.py:169) and the nodes grouped by element, on the device; cached per node_attrs tensor and version."""
     import weakref
-    for ref, ver, e in reversed(_ELEM_CACHE):
+    for ref, ver, g in reversed(_ELEM_CACHE):
         if ref() is node_attrs and ver == node_attrs._version:
-            return e
+            return g
     a = node_attrs.contiguous()
     if a.dtype != torch.float32 or not a.is_cuda:
         raise TypeError('node_attrs must be a float32 CUDA tensor')
-    elem = torch.empty(a.shape[0], dtype=torch.int32, device=a.device)
-    _lib.call('mmk_elem_index', _lib.ptr(a), a.shape[0], a.shape[1], _lib.ptr(elem), _lib.stream_of(a))
-    _ELEM_CACHE.append((weakref.ref(node_attrs), node_attrs._version, elem))
+    N, n_elem = a.shape
+    st = _lib.stream_of(a)
+    elem = torch.empty(N, dtype=torch.int32, device=a.device)
+    erow = torch.empty(n_elem + 1, dtype=torch.int32, device=a.device)
+    perm = torch.empty(N, dtype=torch.int32, device=a.device)
+    _lib.call('mmk_elem_index', _lib.ptr(a), N, n_elem, _lib.ptr(elem), st)
+    nb = _lib.lib().mmk_csr_workspace_bytes(n_elem, N)
+    ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=a.device)
+    _lib.call('mmk_elem_groups', _lib.ptr(elem), N, n_elem, _lib.ptr(erow), _lib.ptr(perm), _lib.ptr(ws), nb, st)
+    g = (elem, erow, perm)
+    _ELEM_CACHE.append((weakref.ref(node_attrs), node_attrs._version, g))
     del _ELEM_CACHE[:-4]
-    return elem
+    return g
 
 
 class _SCFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, elem, op):
+    def forward(ctx, x, erow, perm, op):
         if x.dtype != torch.float32 or not x.is_cuda:
             raise TypeError(f'x must be a float32 CUDA tensor (got {x.dtype} on {x.device})')
-        x = x.contiguous()
+        x = _lib.aligned(x.contiguous())
         N = x.shape[0]
         if x.shape != (N, op.spec.C, op.spec.n_ell):
             raise ValueError(f'x must be [N, {op.spec.C}, {op.spec.n_ell}] (got {tuple(x.shape)})')
+        n_elem = erow.shape[0] - 1
+        if n_elem != op.T.shape[0]:
+            raise ValueError(f'node_attrs has {n_elem} elements, the contraction {op.T.shape[0]}')
         out = torch.empty(N, op.spec.out_dim, device=x.device, dtype=torch.float32)
-        _lib.call('mmk_sc_fwd', op.handle, _lib.ptr(x), _lib.ptr(elem), _lib.ptr(op.T), _lib.ptr(out), N,
-                  _lib.stream_of(x))
-        ctx.save_for_backward(x, elem)
+        _lib.call('mmk_sc_fwd', op.handle, _lib.ptr(x), _lib.ptr(perm), _lib.ptr(erow), n_elem, _lib.ptr(op.T),
+                  _lib.ptr(out), N, _lib.stream_of(x))
+        ctx.save_for_backward(x, erow, perm)
         ctx.op = op
         return out
 
@@ -180,13 +193,13 @@ class _SCFn(torch.autograd.Function):
     def backward(ctx, g):
         if torch.is_grad_enabled():          # only true under create_graph=True
             raise RuntimeError(DOUBLE_BACKWARD_MSG)
-        x, elem = ctx.saved_tensors
+        x, erow, perm = ctx.saved_tensors
         op = ctx.op
         g = g.contiguous()
         gx = torch.empty_like(x)
-        _lib.call('mmk_sc_bwd', op.handle, _lib.ptr(x), _lib.ptr(elem), _lib.ptr(op.T), _lib.ptr(g), _lib.ptr(gx),
-                  x.shape[0], _lib.stream_of(x))
-        return gx, None, None
+        _lib.call('mmk_sc_bwd', op.handle, _lib.ptr(x), _lib.ptr(perm), _lib.ptr(erow), erow.shape[0] - 1,
+                  _lib.ptr(op.T), _lib.ptr(g), _lib.ptr(gx), x.shape[0], _lib.stream_of(x))
+        return gx, None, None, None
 
 
 class CudaSymmetricContraction(torch.nn.Module):
@@ -209,6 +222,13 @@ class CudaSymmetricContraction(torch.nn.Module):
     def handle(self):
         return self._h.value
 
+    def status(self, reset=False):
+        """Error status of this layer's kernels on the current device (0 = ok); synchronises with the device."""
+        import ctypes
+        v = ctypes.c_int(0)
+        _lib.call('mmk_sc_layer_status', self.handle, ctypes.byref(v), int(reset))
+        return v.value
+
     def __deepcopy__(self, memo):
         import copy
         new = self.__class__.__new__(self.__class__)
@@ -220,7 +240,8 @@ class CudaSymmetricContraction(torch.nn.Module):
         return new
 
     def forward(self, x, y):
-        return _SCFn.apply(x, element_index(y), self)
+        _, erow, perm = element_groups(y)
+        return _SCFn.apply(x, erow, perm, self)
 
 
 MetalSymmetricContraction = CudaSymmetricContraction

@@ -35,6 +35,8 @@ CONV_CASES = [
     ('128x0e+128x1o', 3, 160, 5000),
     ('128x0e+128x1o+128x2e', 3, 90, 2000),
     ('96x0e+96x1o', 3, 3, 17),
+    ('64x0e+64x1o', 3, 3000, 90000),
+    ('32x0e+32x1o', 3, 5, 900),
 ]
 
 
@@ -61,6 +63,7 @@ def test_conv_fwd_bwd_matches_oracle(cuda, hidden, lmax, N, E):
     close(gx, rgx, what='gx')
     close(gY, rgY, what='gY')
     close(gW, rgW, what='gW')
+    assert op.status() == 0
     # the unpatched e3nn-style path on the GPU (fp32) agrees too
     with torch.no_grad():
         mji = tp(x.detach()[ei[0].to(cuda)], Y.detach(), W.detach())
@@ -116,6 +119,8 @@ SC_CASES = [
     ('128x0e', 3, 3, 33),
     ('64x0e', 2, 2, 20),
     ('32x0e+32x1o+32x2e', 3, 3, 25),
+    ('128x0e+128x1o', 3, 3, 1001),
+    ('32x0e', 2, 3, 3),
 ]
 
 
@@ -143,6 +148,7 @@ def test_sc_fwd_bwd_matches_oracle(cuda, hidden, lmax, corr, N):
     g = torch.randn_like(out)
     gx, = torch.autograd.grad(out, (x,), g)
     close(gx, sc_ref.sc_bwd(spec, x.detach().cpu(), elem.numpy(), g.cpu()), what='sc gx')
+    assert op.status() == 0
 
 
 def test_double_backward_raises_on_ops(cuda):
