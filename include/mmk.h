@@ -139,7 +139,8 @@ MMK_API int mmk_csr_build_noalloc(const int64_t *index, int64_t n_edges, int64_t
  * for output block q (M_q components, output offset out_off_q = C * sum_{q'<q} M_q'), term t with monomial
  * prod_{i in idx_t} x_i (degree deg_t, indices into the n_ell per-channel components) and first row row_t:
  *   out[b, out_off_q + c*M_q + m] = sum_t T[elem(b), row_t + m, c] * prod_{i in idx_t} x[b, c, i]
- * T is [n_elem, n_rows, C] fp32 on the device (caller-owned). */
+ * T is [n_elem, n_rows, CP] fp32 on the device (caller-owned), CP = C rounded up to a multiple of 4 (zero padded), so
+ * every row chunk the kernels copy with TMA starts on a 16-byte boundary. */
 typedef struct mmk_sc_desc {
     int C;                   /* channels                                                             */
     int n_ell;               /* per-channel feature components, (l_max+1)^2                          */

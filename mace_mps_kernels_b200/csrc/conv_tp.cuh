@@ -9,8 +9,9 @@
 //   * one producer warp streams, edge by edge in CSR order, the rows an edge needs into a STAGES-deep ring of shared
 //     memory with TMA bulk copies (cp.async.bulk, completion counted on a per-stage mbarrier): W[e] (NINS*MUL floats)
 //     plus x[sender] (forward) or grad_out[receiver] (backward), plus Y[e] when its row is 16-byte sized;
-//   * MUL consumer threads (one per channel u) wait for a stage, run the generated per-edge body on their channel's
-//     values, and release the stage back to the producer.
+//   * CG consumer groups of MUL threads (one per channel u) take a node's edges round-robin: each waits for its
+//     edge's stage, runs the generated per-edge body on its channel's values and releases the stage to the producer;
+//     the groups' partial sums of a node are added in shared memory in group order.
 // Nodes are dealt to CTAs round-robin (node = blockIdx.x + k * gridDim.x) so that the CTAs work on a contiguous window
 // of nodes at any time and the gathered rows of their shared neighbours are reused from L2.
 //   forward   node = receiver; out[n] accumulated in registers over the receiver CSR segment, written once:
@@ -26,7 +27,7 @@
 #define X_DIM (XR * MUL)
 #define OUT_DIM (ORR * MUL)
 #define W_DIM (NINS * MUL)
-#define NCW (MUL / 32)                      // consumer warps
+#define NCW (MUL / 32)                      // warps of one consumer group
 #define Y_TMA ((YD * 4) % 16 == 0)         // Y rows are copied with TMA when 16-byte sized
 #define MMK_WAIT_BUDGET (2000000000LL)      // clock64 cycles, ~1 s
 
@@ -146,11 +147,60 @@ __device__ __forceinline__ void drain(u64 *full, u32 issued) {
     for (u32 i = first; i < issued; ++i) mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
 }
 
+// Consumer groups: the CG groups of MUL threads of a CTA take the edges of a node round-robin (edge j of the node ->
+// group j % CG), so one node's edges are worked on by CG*MUL/32 warps at once; their partial sums are added in shared
+// memory in group order (deterministic).  The hand-over buffer has two halves (node parity); red_full[h] completes
+// when groups 1.. have written half h, red_free[h] when group 0 has read it.
+template <int CG, int K>
+__device__ __forceinline__ bool reduce_groups(u64 *red_full, u64 *red_free, float *red, int grp, int u, u32 node_it,
+                                              float (&v)[K]) {
+    if constexpr (CG == 1) {
+        return true;
+    } else {
+        const u32 h = node_it & 1, ph = (node_it >> 1) & 1;
+        float *buf = red + (size_t)h * (CG - 1) * K * MUL;
+        const int lane = threadIdx.x & 31;
+        if (grp > 0) {
+            if (!mbar_wait(&red_free[h], ph ^ 1)) return false;
+            float *dst = buf + (size_t)(grp - 1) * K * MUL + u;
+#pragma unroll
+            for (int i = 0; i < K; ++i) dst[i * MUL] = v[i];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&red_full[h]);
+        } else {
+            if (!mbar_wait(&red_full[h], ph)) return false;
+#pragma unroll
+            for (int q = 0; q < CG - 1; ++q) {
+                const float *src = buf + (size_t)q * K * MUL + u;
+#pragma unroll
+                for (int i = 0; i < K; ++i) v[i] += src[i * MUL];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&red_free[h]);
+        }
+        return true;
+    }
+}
+
+__device__ __forceinline__ void init_barriers(u64 *full, u64 *empty, int stages, u64 *extra, int n_extra, u32 extra_count,
+                                              u64 *extra2, int n_extra2, u32 extra2_count) {
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NCW);
+        }
+        for (int i = 0; i < n_extra; ++i) mbar_init(&extra[i], extra_count);
+        for (int i = 0; i < n_extra2; ++i) mbar_init(&extra2[i], extra2_count);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+}
+
 // ------------------------------------------------------------------------------------------------------------------
 // forward
 // ------------------------------------------------------------------------------------------------------------------
-template <int STAGES>
-__global__ void __launch_bounds__(MUL + 32)
+template <int STAGES, int CG>
+__global__ void __launch_bounds__(CG * MUL + 32)
 mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ senders, float *__restrict__ out, long long n_nodes) {
@@ -158,17 +208,13 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     extern __shared__ __align__(128) float smem[];
     u64 *full = reinterpret_cast<u64 *>(smem + STAGES * STAGE_F);
     u64 *empty = full + STAGES;
+    u64 *red_full = empty + STAGES;                 // [2]
+    u64 *red_free = red_full + 2;                   // [2]
+    float *red = reinterpret_cast<float *>(red_free + 2);   // [2][CG-1][ORR][MUL]
     const int tid = threadIdx.x;
-    if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NCW);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
+    init_barriers(full, empty, STAGES, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
 
-    if (tid >= MUL) {                               // producer warp
+    if (tid >= CG * MUL) {                          // producer warp
         u32 it = 0;
         auto issue = [&](u32 st, long long e, long long s, u64 *bar) {
             float *stage = smem + st * STAGE_F;
@@ -184,17 +230,18 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         return;
     }
 
-    const int u = tid;
-    u32 it = 0;
-    for (long long n = blockIdx.x; n < n_nodes; n += gridDim.x) {
+    const int grp = tid / MUL, u = tid % MUL, lane = tid & 31;
+    u32 it = 0, node_it = 0;
+    for (long long n = blockIdx.x; n < n_nodes; n += gridDim.x, ++node_it) {
         float acc[ORR];
 #pragma unroll
         for (int i = 0; i < ORR; ++i) acc[i] = 0.0f;
         const int p0 = rowptr[n], p1 = rowptr[n + 1];
         for (int p = p0; p < p1; ++p, ++it) {
+            if ((p - p0) % CG != grp) continue;
             const u32 st = it % STAGES, ph = (it / STAGES) & 1;
             if (!mbar_wait(&full[st], ph)) {
-                if ((tid & 31) == 0) atomicExch(&mmk_status, 2);
+                if (lane == 0) atomicExch(&mmk_status, 2);
                 return;
             }
             const float *stage = smem + st * STAGE_F;
@@ -211,18 +258,22 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
                 for (int j = 0; j < YD; ++j) y[j] = __ldg(Y + e * YD + j);
             }
             __syncwarp();
-            if ((tid & 31) == 0) mbar_arrive(&empty[st]);
+            if (lane == 0) mbar_arrive(&empty[st]);
             fwd_edge(xs, y, w, acc);
         }
-        store_out(out + n * OUT_DIM, u, acc);
+        if (!reduce_groups<CG, ORR>(red_full, red_free, red, grp, u, node_it, acc)) {
+            if (lane == 0) atomicExch(&mmk_status, 9);
+            return;
+        }
+        if (grp == 0) store_out(out + n * OUT_DIM, u, acc);
     }
 }
 
 // ------------------------------------------------------------------------------------------------------------------
 // backward
 // ------------------------------------------------------------------------------------------------------------------
-template <int STAGES>
-__global__ void __launch_bounds__(MUL + 32)
+template <int STAGES, int CG>
+__global__ void __launch_bounds__(CG * MUL + 32)
 mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const float *__restrict__ g, const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ receivers, float *__restrict__ gx, float *__restrict__ gY,
@@ -231,21 +282,20 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     extern __shared__ __align__(128) float smem[];
     u64 *full = reinterpret_cast<u64 *>(smem + STAGES * STAGE_F);
     u64 *empty = full + STAGES;
-    u64 *red = empty + STAGES;                                    // [2] consumer warps' gY partials are in
-    float *part = reinterpret_cast<float *>(red + 2);             // [2][NCW][16] channel-sum partials of gY
+    u64 *red_full = empty + STAGES;                 // [2]   gx hand-over between groups
+    u64 *red_free = red_full + 2;                   // [2]
+    u64 *ybar = red_free + 2;                       // [CG][2]  each group's warps have put their gY partials
+    float *part = reinterpret_cast<float *>(ybar + 2 * CG);      // [CG][2][NCW][16]
+    float *red = part + CG * 2 * NCW * 16;                       // [2][CG-1][XR][MUL]
     const int tid = threadIdx.x;
+    init_barriers(full, empty, STAGES, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
     if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NCW);
-        }
-        mbar_init(&red[0], NCW);
-        mbar_init(&red[1], NCW);
+        for (int i = 0; i < 2 * CG; ++i) mbar_init(&ybar[i], NCW);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
 
-    if (tid >= MUL) {
+    if (tid >= CG * MUL) {
         u32 it = 0;
         auto issue = [&](u32 st, long long e, long long r, u64 *bar) {
             float *stage = smem + st * STAGE_F;
@@ -261,15 +311,16 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         return;
     }
 
-    const int u = tid, warp = tid >> 5, lane = tid & 31;
-    u32 it = 0;
-    for (long long s = blockIdx.x; s < n_nodes; s += gridDim.x) {
+    const int grp = tid / MUL, u = tid % MUL, warp = u >> 5, lane = tid & 31;
+    u32 it = 0, node_it = 0, mine = 0;               // mine: edges this group has handled (gY buffer parity)
+    for (long long s = blockIdx.x; s < n_nodes; s += gridDim.x, ++node_it) {
         float xs[XR], gxa[XR];
         load_x(x + s * X_DIM, u, xs);
 #pragma unroll
         for (int i = 0; i < XR; ++i) gxa[i] = 0.0f;
         const int p0 = rowptr[s], p1 = rowptr[s + 1];
         for (int p = p0; p < p1; ++p, ++it) {
+            if ((p - p0) % CG != grp) continue;
             const u32 st = it % STAGES, ph = (it / STAGES) & 1;
             if (!mbar_wait(&full[st], ph)) {
                 if (lane == 0) atomicExch(&mmk_status, 4);
@@ -299,13 +350,14 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
                 for (int k = 0; k < NINS; ++k) gwe[k * MUL] = gw[k];
             }
             if (gY != nullptr) {
-                const u32 b = it & 1;
-                float *pb = part + b * (NCW * 16);
+                const u32 b = mine & 1;
+                u64 *yb = &ybar[grp * 2 + b];
+                float *pb = part + ((size_t)grp * 2 + b) * (NCW * 16);
                 const float v = warp_transpose_reduce16(gy);
                 if ((lane & 1) == 0) pb[warp * 16 + (lane >> 1)] = v;
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&red[b]);
-                if (!mbar_wait(&red[b], (it >> 1) & 1)) {
+                if (lane == 0) mbar_arrive(yb);
+                if (!mbar_wait(yb, (mine >> 1) & 1)) {
                     if (lane == 0) atomicExch(&mmk_status, 5);
                     return;
                 }
@@ -315,10 +367,15 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
                     for (int q = 0; q < NCW; ++q) t += pb[q * 16 + u];
                     gY[e * YD + u] = t;
                 }
-                // edge it+1 uses the other half; the writes of edge it+2 into this half come after every warp passed
-                // red[b ^ 1] at edge it+1, i.e. after these reads
+                // this group's next edge uses the other half; its writes into this half two edges later come after
+                // every warp of the group passed the other half's barrier, i.e. after these reads
             }
+            ++mine;
         }
-        if (gx != nullptr) store_x(gx + s * X_DIM, u, gxa);
+        if (!reduce_groups<CG, XR>(red_full, red_free, red, grp, u, node_it, gxa)) {
+            if (lane == 0) atomicExch(&mmk_status, 9);
+            return;
+        }
+        if (gx != nullptr && grp == 0) store_x(gx + s * X_DIM, u, gxa);
     }
 }

@@ -208,7 +208,12 @@ class CudaSymmetricContraction(torch.nn.Module):
     def __init__(self, sc, device='cuda', spec=None):
         super().__init__()
         self.spec = SCSpec(sc) if spec is None else spec
-        self.register_buffer('T', self.spec.T.to(device).contiguous())
+        # the kernels read T with a channel stride rounded up to 4 floats (16-byte rows for the TMA copies)
+        T = self.spec.T
+        cp = (T.shape[2] + 3) // 4 * 4
+        if cp != T.shape[2]:
+            T = torch.nn.functional.pad(T, (0, cp - T.shape[2]))
+        self.register_buffer('T', T.to(device).contiguous())
         self._h = _LayerHandle('mmk_sc_layer_create', 'mmk_sc_layer_destroy', self.spec.descriptor())
         self.irreps_in = getattr(sc, 'irreps_in', None)
         self.irreps_out = getattr(sc, 'irreps_out', None)
