@@ -10,10 +10,19 @@ rank runs its own structure (seed = rank): weak scaling, the only collective is 
 One step = one energy + force call (model forward + autograd backward through the patched kernels).  Inputs are
 much smaller than L2, so L2 is flushed (256 MB write) before every timed step, outside the CUDA-event interval.
 
+The timed step is a replay of the whole E+F call captured in a CUDA graph (GraphedEnergyForces); the eager time is
+reported beside it.
+
 Printed JSON (rank 0): value = atoms x ranks / step time (max over ranks, CUDA events); e2e = the same through the
 public API with host inputs (pinned H2D copies of the graph and a D2H copy of the forces inside the timed interval);
-roofline = the dominant kernel's algorithmic bytes / its CUDA-event duration against the measured HBM copy
-bandwidth; cpu_baseline = the unpatched e3nn-path model on the host cores (rank 0, N = 1 only).
+ops = every patched op's forward and backward kernel on the step's own inputs, launched through the C ABI ('cold':
+1 GiB L2 flush before each launch; 'hot': back to back); roofline = the dominant one's algorithmic bytes / its
+CUDA-event duration against the measured HBM copy bandwidth; ops_large / roofline_large = the same ops of the
+configs[4] architecture on a bulk Cu supercell far larger than L2 (symmetric contraction against a measured FP32 GEMM
+peak); cpu_baseline = the unpatched e3nn-path model on the host cores (rank 0, N = 1 only).
+
+Profiling entry points (ncu --profile-from-start off ...): --profile step (three graph replays of the E+F step),
+--profile ops [--large-cells K] (one launch of every large-system op).
 """
 from __future__ import annotations
 
@@ -149,47 +158,54 @@ def conv_bytes(spec, N, E):
     return fwd, bwd
 
 
-def time_ops(calls, reps, flush):
-    """CUDA-event time of each patched op's forward and backward kernel, launched directly through the C ABI with
-    preallocated outputs; a 256 MB L2 flush is enqueued before every launch, which also hides the host launch."""
+def conv_case(mod, x, Y, W, ei, name):
+    """(fwd, bwd) closures launching one conv layer's kernels through the C ABI on preallocated buffers."""
     from mace_mps_kernels_b200.conv import graph_csr
-    res = []
-    stream = torch.cuda.current_stream()
-    st = _lib.stream_of(torch.empty(1, device='cuda'))
     P = _lib.ptr
-    n_conv = n_sc = 0
-    for mod, args, out in calls:
-        if isinstance(mod, CudaConvTP):
-            x, Y, W, ei = (a.contiguous() for a in args)
-            N, E = x.shape[0], Y.shape[0]
-            rr, re_, sr, se = graph_csr(ei, N)
-            o = torch.empty_like(out)
-            g = torch.randn_like(out)
-            gx, gY, gW = torch.empty_like(x), torch.empty_like(Y), torch.empty_like(W)
-            recv = ei.data_ptr() + E * 8
-            fwd = lambda: _lib.call('mmk_conv_fwd', mod.handle, P(x), P(Y), P(W), P(rr), P(re_), P(ei), P(o), N, E, st)
-            bwd = lambda: _lib.call('mmk_conv_bwd', mod.handle, P(x), P(Y), P(W), P(g), P(sr), P(se), recv, P(gx),
-                                    P(gY), P(gW), N, E, st)
-            kind, name = 'conv', f'conv_tp[{n_conv}]'
-            n_conv += 1
-        else:
-            from mace_mps_kernels_b200.symmetric import element_groups
-            x, attrs = (a.contiguous() for a in args)
-            N = x.shape[0]
-            _, erow, perm = element_groups(attrs)
-            ne = erow.shape[0] - 1
-            o = torch.empty_like(out)
-            g = torch.randn_like(out)
-            gx = torch.empty_like(x)
-            fwd = lambda: _lib.call('mmk_sc_fwd', mod.handle, P(x), P(perm), P(erow), ne, P(mod.T), P(o), N, st)
-            bwd = lambda: _lib.call('mmk_sc_bwd', mod.handle, P(x), P(perm), P(erow), ne, P(mod.T), P(g), P(gx), N, st)
-            kind, name = 'sc', f'symcon[{n_sc}]'
-            n_sc += 1
-        times = {}
-        for tag, fn in (('fwd', fwd), ('bwd', bwd)):
+    st = _lib.stream_of(x)
+    N, E = x.shape[0], Y.shape[0]
+    rr, re_, sr, se = graph_csr(ei, N)
+    o = torch.empty(N, mod.spec.out_dim, device=x.device)
+    g = torch.randn_like(o)
+    gx, gY, gW = torch.empty_like(x), torch.empty_like(Y), torch.empty_like(W)
+    recv = ei.data_ptr() + E * 8
+    fwd = lambda: _lib.call('mmk_conv_fwd', mod.handle, P(x), P(Y), P(W), P(rr), P(re_), P(ei), P(o), N, E, st)
+    bwd = lambda: _lib.call('mmk_conv_bwd', mod.handle, P(x), P(Y), P(W), P(g), P(sr), P(se), recv, P(gx), P(gY),
+                            P(gW), N, E, st)
+    bf, bb = conv_bytes(mod.spec, N, E)
+    return dict(op=name, kind='conv', N=N, E=E, nnz=mod.spec.nnz, fwd=fwd, bwd=bwd, fwd_bytes=bf, bwd_bytes=bb,
+                keep=(o, g, gx, gY, gW, rr, re_, sr, se))
+
+
+def sc_case(mod, x, attrs, name):
+    from mace_mps_kernels_b200.symmetric import element_groups
+    P = _lib.ptr
+    st = _lib.stream_of(x)
+    N = x.shape[0]
+    _, erow, perm = element_groups(attrs)
+    ne = erow.shape[0] - 1
+    o = torch.empty(N, mod.spec.out_dim, device=x.device)
+    g = torch.randn_like(o)
+    gx = torch.empty_like(x)
+    fwd = lambda: _lib.call('mmk_sc_fwd', mod.handle, P(x), P(perm), P(erow), ne, P(mod.T), P(o), N, st)
+    bwd = lambda: _lib.call('mmk_sc_bwd', mod.handle, P(x), P(perm), P(erow), ne, P(mod.T), P(g), P(gx), N, st)
+    ff, fb = mod.spec.flops()
+    C = mod.spec.C
+    return dict(op=name, kind='sc', N=N, terms=mod.spec.n_terms, fwd=fwd, bwd=bwd, fwd_flops=ff * N * C,
+                bwd_flops=fb * N * C, keep=(o, g, gx, erow, perm))
+
+
+def time_cases(cases, reps, flush):
+    """Per launch, CUDA events: 'cold' = L2 flushed (1 GiB write) before each launch, which also lets the host enqueue
+    the launch before the GPU reaches the start event; 'hot' = reps launches back to back between two events."""
+    res = []
+    for c in cases:
+        out = {k: v for k, v in c.items() if k not in ('fwd', 'bwd', 'keep')}
+        for tag in ('fwd', 'bwd'):
+            fn = c[tag]
             ts = []
             for r in range(reps + 2):
-                flush(stream)
+                flush()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
                 fn()
@@ -197,18 +213,86 @@ def time_ops(calls, reps, flush):
                 e1.synchronize()
                 if r >= 2:
                     ts.append(e0.elapsed_time(e1) * 1e3)
-            times[tag] = float(np.median(ts))
-        if kind == 'conv':
-            bf, bb = conv_bytes(mod.spec, N, E)
-            res.append(dict(op=name, kind=kind, N=N, E=E, nnz=mod.spec.nnz, fwd_us=times['fwd'],
-                            bwd_us=times['bwd'], fwd_bytes=bf, bwd_bytes=bb,
-                            fwd_gbs=bf / times['fwd'] * 1e-3, bwd_gbs=bb / times['bwd'] * 1e-3))
-        else:
-            ff, fb = mod.spec.flops()
-            C = mod.spec.C
-            res.append(dict(op=name, kind=kind, N=N, terms=mod.spec.n_terms, fwd_us=times['fwd'],
-                            bwd_us=times['bwd'], fwd_flops=ff * N * C, bwd_flops=fb * N * C))
+            out[f'{tag}_us'] = float(np.median(ts))
+            flush()
+            fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            e1.synchronize()
+            out[f'{tag}_hot_us'] = e0.elapsed_time(e1) * 1e3 / reps
+            if c['kind'] == 'conv':
+                out[f'{tag}_gbs'] = c[f'{tag}_bytes'] / out[f'{tag}_us'] * 1e-3
+            else:
+                out[f'{tag}_tflops'] = c[f'{tag}_flops'] / out[f'{tag}_us'] * 1e-6
+        res.append(out)
     return res
+
+
+def step_cases(model, batch):
+    """The patched ops of one E+F call of ``model`` on ``batch``, with the inputs they saw."""
+    calls = capture_op_inputs(model, batch)
+    cases, nc, ns = [], 0, 0
+    for mod, args, out in calls:
+        if isinstance(mod, CudaConvTP):
+            x, Y, W, ei = (a.contiguous() for a in args)
+            cases.append(conv_case(mod, x, Y, W, ei, f'conv_tp[{nc}]'))
+            nc += 1
+        else:
+            x, attrs = (a.contiguous() for a in args)
+            cases.append(sc_case(mod, x, attrs, f'symcon[{ns}]'))
+            ns += 1
+    return cases
+
+
+LARGE_CELLS = 16
+
+
+def large_cases(dev, cells=LARGE_CELLS):
+    """configs[4]'s architecture (128x0e+128x1o+128x2e, l_max 3, correlation 3) on a bulk fcc Cu supercell of
+    LARGE_CELLS^3 conventional cells (Morton-ordered atoms, r_max 5 A): per-op inputs far larger than L2."""
+    torch.manual_seed(1)
+    model = standin.make_model('128x0e+128x1o+128x2e', 3, 3, seed=0, elements=[29, 30, 31, 32]).to(dev)
+    patch_model(model, verbose=False)
+    st = standin.fcc_bulk('Cu', 3.61, cells, seed=0, jitter=0.1)
+    st = st.permuted(standin.structures.morton_order(st.positions, st.cell))
+    i, j, _ = standin.neighbor_list(st.positions, st.cell, st.pbc, 5.0)
+    ei = torch.from_numpy(np.stack([i, j])).to(dev)
+    N, E = len(st), ei.shape[1]
+    cases = []
+    for k, blk in enumerate(model.interactions):
+        sp = blk.conv_tp.spec
+        x = torch.randn(N, sp.x_dim, device=dev)
+        Y = torch.randn(E, sp.y_dim, device=dev)
+        W = torch.randn(E, sp.w_dim, device=dev)
+        cases.append(conv_case(blk.conv_tp, x, Y, W, ei, f'conv_tp[{k}] Cu{cells}^3'))
+    attrs = torch.zeros(N, 4, device=dev)
+    attrs[:, 0] = 1.0
+    for k, prod in enumerate(model.products):
+        sc = prod.symmetric_contractions
+        x = torch.randn(N, sc.spec.C, sc.spec.n_ell, device=dev)
+        cases.append(sc_case(sc, x, attrs, f'symcon[{k}] Cu{cells}^3'))
+    return cases, dict(atoms=N, edges=E, model='128x0e+128x1o+128x2e l_max 3 corr 3')
+
+
+def fp32_peak(dev):
+    """Measured FP32 (no TF32) GEMM throughput, TFLOP/s: the FP32-issue roof for the symmetric contraction."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    a = torch.randn(8192, 8192, device=dev)
+    b = torch.randn(8192, 8192, device=dev)
+    for _ in range(2):
+        a @ b
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        a @ b
+    e1.record()
+    e1.synchronize()
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    return 2 * 8192 ** 3 * 5 / (e0.elapsed_time(e1) * 1e-3) / 1e12
 
 
 def cpu_baseline(n_steps_cap=5, budget_s=20.0):
@@ -236,8 +320,14 @@ def main():
     ap.add_argument('--steps', type=int, default=300)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--op-reps', type=int, default=10)
+    ap.add_argument('--op-reps', type=int, default=20)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-large', action='store_true', help='skip the large-system per-op measurement')
+    ap.add_argument('--large-cells', type=int, default=LARGE_CELLS, help='fcc Cu supercell edge of the large case')
+    ap.add_argument('--profile', choices=['step', 'ops'], default=None,
+                    help='run only the region to profile between cudaProfilerStart/Stop (for ncu '
+                         '--profile-from-start off): three replays of the graphed E+F step, or one launch of every '
+                         'large-system op')
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
 
@@ -263,7 +353,7 @@ def main():
     st, host_batch = workload(rank)
     n_atoms, n_edges = len(st), int(host_batch['edge_index'].shape[1])
     batch = standin.to_device(host_batch, dev)
-    flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)   # 2x L2, between steps
     e_all = torch.zeros(world, device=dev)
 
     # eager E+F (for reference in the JSON line), then the CUDA-graphed E+F that is timed
@@ -276,6 +366,28 @@ def main():
     torch.cuda.synchronize()
     eager_ms = (time.perf_counter() - t0) / 5 * 1e3
     graphed = GraphedEnergyForces(model, batch)
+    if a.profile == 'step':
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        for _ in range(3):
+            graphed()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        return
+    if a.profile == 'ops':
+        cases, info = large_cases(dev, a.large_cells)
+        for c in cases:                              # warm (module load, CSR) outside the profiled region
+            c['fwd']()
+            c['bwd']()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        for c in cases:
+            c['fwd']()
+            c['bwd']()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps(info))
+        return
 
     def step(b=None):
         E, F = graphed(b)
@@ -343,19 +455,35 @@ def main():
     ms_e2e = float(t.item())
 
     # ---- per-op kernel timing (dominant kernel -> roofline) -----------------------------------------------------
-    calls = capture_op_inputs(model, batch)
-    ops = time_ops(calls, a.op_reps, lambda s: flush_l2(flush_buf))
+    big_flush = torch.empty(1024 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush = lambda: flush_l2(big_flush)
+    ops = time_cases(step_cases(model, batch), a.op_reps, flush)
     hbm, hbm_kind = peaks()
-    conv_ops = [o for o in ops if o['kind'] == 'conv']
-    dom = max(conv_ops, key=lambda o: o['fwd_us'] + o['bwd_us'])
-    dom_bytes = dom['fwd_bytes'] + dom['bwd_bytes']
-    dom_us = dom['fwd_us'] + dom['bwd_us']
-    achieved = dom_bytes / (dom_us * 1e-6) / 1e9
-    roofline = {'kernel': f"{dom['op']} fwd+bwd (mmk_conv_fwd_kernel + mmk_conv_bwd_kernel)", 'bound': 'hbm',
-                'achieved': round(achieved, 1), 'peak': hbm, 'peak_kind': hbm_kind, 'unit': 'GB/s',
-                'frac': round(achieved / hbm, 4), 'traffic': None,
-                'algorithmic_bytes_per_launch': dom_bytes, 'us_per_launch': round(dom_us, 2),
-                'note': 'fits in L2 at this size: latency-bound; see profiles/ for the large-system sweep'}
+
+    def conv_roof(o, note):
+        b = o['fwd_bytes'] + o['bwd_bytes']
+        us = o['fwd_us'] + o['bwd_us']
+        ach = b / (us * 1e-6) / 1e9
+        return {'kernel': f"{o['op']} fwd+bwd (mmk_conv_fwd_kernel + mmk_conv_bwd_kernel), N={o['N']} E={o['E']}",
+                'bound': 'hbm', 'achieved': round(ach, 1), 'peak': hbm, 'peak_kind': hbm_kind, 'unit': 'GB/s',
+                'frac': round(ach / hbm, 4), 'traffic': None, 'algorithmic_bytes_per_launch': b,
+                'us_per_launch': round(us, 2), 'note': note}
+
+    dom = max((o for o in ops if o['kind'] == 'conv'), key=lambda o: o['fwd_us'] + o['bwd_us'])
+    roofline = conv_roof(dom, 'dominant kernel of the timed E+F step; its data fits in L2, so it is latency-bound '
+                              '(cold: L2 flushed before the launch)')
+    large, roof_large, fp32 = None, None, None
+    if not a.no_large and rank == 0:
+        del big_flush
+        cases, info = large_cases(dev, a.large_cells)
+        large = dict(info, ops=time_cases(cases, max(3, a.op_reps // 4), flush))
+        del cases
+        big = max((o for o in large['ops'] if o['kind'] == 'conv'), key=lambda o: o['fwd_us'] + o['bwd_us'])
+        roof_large = conv_roof(big, 'inputs far larger than L2 (bulk Cu, configs[4] architecture)')
+        fp32 = fp32_peak(dev)
+        for o in large['ops'] + ops:
+            if o['kind'] == 'sc':
+                o['fp32_peak_tflops'] = round(fp32, 1)
 
     if rank == 0:
         cpu = None
@@ -370,12 +498,18 @@ def main():
                     'd2h_bytes_per_step': d2h, 'ms_per_step': round(ms_e2e, 4)},
             'roofline': roofline, 'cpu_baseline': cpu, 'gpu_launches': launches, 'clocks': clk.summary(),
             'eager_ms_per_step': round(eager_ms, 3),
-            'ops': [{k: (round(v, 2) if isinstance(v, float) else v) for k, v in o.items()} for o in ops],
+            'ops': [rounded(o) for o in ops],
+            'roofline_large': roof_large,
+            'ops_large': None if large is None else dict(large, ops=[rounded(o) for o in large['ops']]),
         }
         print(json.dumps(res))
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def rounded(o):
+    return {k: (round(v, 2) if isinstance(v, float) else v) for k, v in o.items()}
 
 
 def reference_arm(a, rank, world):
