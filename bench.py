@@ -474,7 +474,6 @@ def main():
                               '(cold: L2 flushed before the launch)')
     large, roof_large, fp32 = None, None, None
     if not a.no_large and rank == 0:
-        del big_flush
         cases, info = large_cases(dev, a.large_cells)
         large = dict(info, ops=time_cases(cases, max(3, a.op_reps // 4), flush))
         del cases

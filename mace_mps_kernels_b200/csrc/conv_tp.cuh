@@ -12,8 +12,8 @@
 //   * CG consumer groups of MUL threads (one per channel u) take a node's edges round-robin: each waits for its
 //     edge's stage, runs the generated per-edge body on its channel's values and releases the stage to the producer;
 //     the groups' partial sums of a node are added in shared memory in group order.
-// Nodes are dealt to CTAs round-robin (node = blockIdx.x + k * gridDim.x) so that the CTAs work on a contiguous window
-// of nodes at any time and the gathered rows of their shared neighbours are reused from L2.
+// Each CTA owns a contiguous range of nodes (a compact domain when atoms are ordered along a space-filling curve), so
+// consecutive nodes gather mostly the same neighbour rows (L2 hits) and the CTA's edges form one stretch of the CSR.
 //   forward   node = receiver; out[n] accumulated in registers over the receiver CSR segment, written once:
 //             deterministic, no atomics.
 //   backward  node = sender; x[s] in registers; per edge gW[e, :, u] (coalesced over u) and gY[e, :] (channel sum:
@@ -107,32 +107,45 @@ __device__ __forceinline__ float warp_transpose_reduce16(float (&v)[16]) {
     return v[0];
 }
 
-// Producer: issue the TMA copies of every edge of the CTA's nodes, in the consumers' order.  All 32 lanes walk the
-// loop (they fetch edge ids 32 at a time); lane 0 waits for free stages and issues.  Returns false on a timeout.
+// Work split: CTA b owns the contiguous node range [b*N/G, (b+1)*N/G) (G = gridDim.x).  With atoms ordered along a
+// space-filling curve a range is a compact domain, so consecutive nodes of a CTA gather mostly the same neighbour rows
+// (L2 hits), and the CTA's edges are one contiguous stretch of the CSR.
+__device__ __forceinline__ void node_range(long long n_nodes, long long &n0, long long &n1) {
+    n0 = (long long)blockIdx.x * n_nodes / gridDim.x;
+    n1 = ((long long)blockIdx.x + 1) * n_nodes / gridDim.x;
+}
+
+// Producer: stream the TMA copies of the CTA's edges [rowptr[n0], rowptr[n1]) in CSR order.  All 32 lanes walk the
+// loop: they fetch the edge ids (and the gathered node of each edge) 32 at a time, one batch ahead, so the index
+// loads overlap the issue of the current batch; lane 0 waits for free stages and issues.  False on a timeout.
 template <int STAGES, class Issue>
 __device__ __forceinline__ bool produce(const int *__restrict__ rowptr, const int *__restrict__ eids,
-                                        const long long *__restrict__ other, long long n_nodes, u64 *full, u64 *empty,
-                                        u32 &it, Issue issue) {
+                                        const long long *__restrict__ other, long long n0, long long n1, u64 *full,
+                                        u64 *empty, u32 &it, Issue issue) {
     const int lane = threadIdx.x & 31;
-    for (long long n = blockIdx.x; n < n_nodes; n += gridDim.x) {
-        const int p0 = rowptr[n], p1 = rowptr[n + 1];
-        for (int q = p0; q < p1; q += 32) {
-            long long e = 0, o = 0;
-            if (q + lane < p1) {
-                e = eids[q + lane];
-                o = other[e];
-            }
-            const int cnt = min(32, p1 - q);
-            for (int j = 0; j < cnt; ++j, ++it) {
-                const long long ej = __shfl_sync(0xffffffffu, e, j);
-                const long long oj = __shfl_sync(0xffffffffu, o, j);
-                const u32 st = it % STAGES, ph = (it / STAGES) & 1;
-                bool ok = true;
-                if (lane == 0) ok = mbar_wait(&empty[st], ph ^ 1);
-                if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return false;
-                if (lane == 0) issue(st, ej, oj, &full[st]);
-                __syncwarp();
-            }
+    if (n0 >= n1) return true;
+    const int q0 = rowptr[n0], q1 = rowptr[n1];
+    long long e_next = 0, o_next = 0;
+    if (q0 + lane < q1) {
+        e_next = eids[q0 + lane];
+        o_next = other[e_next];
+    }
+    for (int q = q0; q < q1; q += 32) {
+        const long long e = e_next, o = o_next;
+        if (q + 32 + lane < q1) {                  // next batch: in flight while this one is issued
+            e_next = eids[q + 32 + lane];
+            o_next = other[e_next];
+        }
+        const int cnt = min(32, q1 - q);
+        for (int j = 0; j < cnt; ++j, ++it) {
+            const long long ej = __shfl_sync(0xffffffffu, e, j);
+            const long long oj = __shfl_sync(0xffffffffu, o, j);
+            const u32 st = it % STAGES, ph = (it / STAGES) & 1;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&empty[st], ph ^ 1);
+            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return false;
+            if (lane == 0) issue(st, ej, oj, &full[st]);
+            __syncwarp();
         }
     }
     return true;
@@ -204,7 +217,7 @@ __global__ void __launch_bounds__(CG * MUL + 32)
 mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ senders, float *__restrict__ out, long long n_nodes) {
-    constexpr u32 STAGE_F = W_DIM + X_DIM + 16;     // floats per stage: W row | x row | Y row (padded to 16)
+    constexpr u32 STAGE_F = W_DIM + X_DIM + 20;     // floats per stage: W row | x row | Y row (16) | edge id (4)
     extern __shared__ __align__(128) float smem[];
     u64 *full = reinterpret_cast<u64 *>(smem + STAGES * STAGE_F);
     u64 *empty = full + STAGES;
@@ -218,12 +231,15 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         u32 it = 0;
         auto issue = [&](u32 st, long long e, long long s, u64 *bar) {
             float *stage = smem + st * STAGE_F;
+            *reinterpret_cast<long long *>(stage + W_DIM + X_DIM + 16) = e;       // released by the arrive below
             mbar_arrive_expect_tx(bar, (W_DIM + X_DIM) * 4 + (Y_TMA ? YD * 4 : 0));
             bulk_g2s(stage, W + e * W_DIM, W_DIM * 4, bar);
             bulk_g2s(stage + W_DIM, x + s * X_DIM, X_DIM * 4, bar);
             if constexpr (Y_TMA) bulk_g2s(stage + W_DIM + X_DIM, Y + e * YD, YD * 4, bar);
         };
-        if (!produce<STAGES>(rowptr, eids, senders, n_nodes, full, empty, it, issue)) {
+        long long n0, n1;
+        node_range(n_nodes, n0, n1);
+        if (!produce<STAGES>(rowptr, eids, senders, n0, n1, full, empty, it, issue)) {
             if ((tid & 31) == 0) atomicExch(&mmk_status, 1);
             drain<STAGES>(full, it);
         }
@@ -232,7 +248,9 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
 
     const int grp = tid / MUL, u = tid % MUL, lane = tid & 31;
     u32 it = 0, node_it = 0;
-    for (long long n = blockIdx.x; n < n_nodes; n += gridDim.x, ++node_it) {
+    long long n0, n1;
+    node_range(n_nodes, n0, n1);
+    for (long long n = n0; n < n1; ++n, ++node_it) {
         float acc[ORR];
 #pragma unroll
         for (int i = 0; i < ORR; ++i) acc[i] = 0.0f;
@@ -253,7 +271,7 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
 #pragma unroll
                 for (int j = 0; j < YD; ++j) y[j] = stage[W_DIM + X_DIM + j];
             } else {
-                const long long e = eids[p];
+                const long long e = *reinterpret_cast<const long long *>(stage + W_DIM + X_DIM + 16);
 #pragma unroll
                 for (int j = 0; j < YD; ++j) y[j] = __ldg(Y + e * YD + j);
             }
@@ -278,33 +296,32 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
                     const float *__restrict__ g, const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ receivers, float *__restrict__ gx, float *__restrict__ gY,
                     float *__restrict__ gW, long long n_nodes) {
-    constexpr u32 STAGE_F = W_DIM + OUT_DIM + 16;   // W row | grad_out row | Y row (padded to 16)
+    constexpr u32 STAGE_F = W_DIM + OUT_DIM + 20;   // W row | grad_out row | Y row (16) | edge id (4)
     extern __shared__ __align__(128) float smem[];
     u64 *full = reinterpret_cast<u64 *>(smem + STAGES * STAGE_F);
     u64 *empty = full + STAGES;
     u64 *red_full = empty + STAGES;                 // [2]   gx hand-over between groups
     u64 *red_free = red_full + 2;                   // [2]
-    u64 *ybar = red_free + 2;                       // [CG][2]  each group's warps have put their gY partials
-    float *part = reinterpret_cast<float *>(ybar + 2 * CG);      // [CG][2][NCW][16]
-    float *red = part + CG * 2 * NCW * 16;                       // [2][CG-1][XR][MUL]
+    float *part = reinterpret_cast<float *>(red_free + 2);       // [STAGES][NCW][16] gY partials of each warp
+    int *arrived = reinterpret_cast<int *>(part + STAGES * NCW * 16);   // [STAGES] warps done with the stage's gY
+    float *red = reinterpret_cast<float *>(arrived + STAGES);    // [2][CG-1][XR][MUL]
     const int tid = threadIdx.x;
+    for (int i = tid; i < STAGES; i += blockDim.x) arrived[i] = 0;
     init_barriers(full, empty, STAGES, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
-    if (tid == 0) {
-        for (int i = 0; i < 2 * CG; ++i) mbar_init(&ybar[i], NCW);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
 
     if (tid >= CG * MUL) {
         u32 it = 0;
         auto issue = [&](u32 st, long long e, long long r, u64 *bar) {
             float *stage = smem + st * STAGE_F;
+            *reinterpret_cast<long long *>(stage + W_DIM + OUT_DIM + 16) = e;     // released by the arrive below
             mbar_arrive_expect_tx(bar, (W_DIM + OUT_DIM) * 4 + (Y_TMA ? YD * 4 : 0));
             bulk_g2s(stage, W + e * W_DIM, W_DIM * 4, bar);
             bulk_g2s(stage + W_DIM, g + r * OUT_DIM, OUT_DIM * 4, bar);
             if constexpr (Y_TMA) bulk_g2s(stage + W_DIM + OUT_DIM, Y + e * YD, YD * 4, bar);
         };
-        if (!produce<STAGES>(rowptr, eids, receivers, n_nodes, full, empty, it, issue)) {
+        long long n0, n1;
+        node_range(n_nodes, n0, n1);
+        if (!produce<STAGES>(rowptr, eids, receivers, n0, n1, full, empty, it, issue)) {
             if ((tid & 31) == 0) atomicExch(&mmk_status, 3);
             drain<STAGES>(full, it);
         }
@@ -312,8 +329,10 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     }
 
     const int grp = tid / MUL, u = tid % MUL, warp = u >> 5, lane = tid & 31;
-    u32 it = 0, node_it = 0, mine = 0;               // mine: edges this group has handled (gY buffer parity)
-    for (long long s = blockIdx.x; s < n_nodes; s += gridDim.x, ++node_it) {
+    u32 it = 0, node_it = 0;
+    long long n0, n1;
+    node_range(n_nodes, n0, n1);
+    for (long long s = n0; s < n1; ++s, ++node_it) {
         float xs[XR], gxa[XR];
         load_x(x + s * X_DIM, u, xs);
 #pragma unroll
@@ -326,8 +345,8 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
                 if (lane == 0) atomicExch(&mmk_status, 4);
                 return;
             }
-            const long long e = eids[p];
             const float *stage = smem + st * STAGE_F;
+            const long long e = *reinterpret_cast<const long long *>(stage + W_DIM + OUT_DIM + 16);
             float y[YD], w[NINS], go[ORR], gw[NINS], gy[16];
 #pragma unroll
             for (int k = 0; k < NINS; ++k) w[k] = stage[k * MUL + u];
@@ -339,8 +358,6 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
 #pragma unroll
                 for (int j = 0; j < YD; ++j) y[j] = __ldg(Y + e * YD + j);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
 #pragma unroll
             for (int j = 0; j < 16; ++j) gy[j] = 0.0f;
             bwd_edge(xs, y, w, go, gxa, gw, gy);
@@ -350,27 +367,31 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
                 for (int k = 0; k < NINS; ++k) gwe[k * MUL] = gw[k];
             }
             if (gY != nullptr) {
-                const u32 b = mine & 1;
-                u64 *yb = &ybar[grp * 2 + b];
-                float *pb = part + ((size_t)grp * 2 + b) * (NCW * 16);
+                // channel sum of gY[e]: each warp reduces its 32 channels in registers and leaves 16 partials in the
+                // stage's slot; the warp that finishes last adds the NCW partials in warp order (deterministic),
+                // writes gY[e] and clears the counter.  The stage is released only afterwards, so the slot is free.
+                float *pb = part + (size_t)st * NCW * 16;
                 const float v = warp_transpose_reduce16(gy);
                 if ((lane & 1) == 0) pb[warp * 16 + (lane >> 1)] = v;
                 __syncwarp();
-                if (lane == 0) mbar_arrive(yb);
-                if (!mbar_wait(yb, (mine >> 1) & 1)) {
-                    if (lane == 0) atomicExch(&mmk_status, 5);
-                    return;
+                int last = 0;
+                if (lane == 0) {
+                    __threadfence_block();
+                    last = atomicAdd(&arrived[st], 1) == NCW - 1;
+                    if (last) __threadfence_block();
                 }
-                if (u < YD) {
-                    float t = 0.0f;
+                if (__shfl_sync(0xffffffffu, last, 0)) {
+                    if (lane < YD) {
+                        float t = 0.0f;
 #pragma unroll
-                    for (int q = 0; q < NCW; ++q) t += pb[q * 16 + u];
-                    gY[e * YD + u] = t;
+                        for (int q = 0; q < NCW; ++q) t += pb[q * 16 + lane];
+                        gY[e * YD + lane] = t;
+                    }
+                    if (lane == 0) arrived[st] = 0;
                 }
-                // this group's next edge uses the other half; its writes into this half two edges later come after
-                // every warp of the group passed the other half's barrier, i.e. after these reads
             }
-            ++mine;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
         }
         if (!reduce_groups<CG, XR>(red_full, red_free, red, grp, u, node_it, gxa)) {
             if (lane == 0) atomicExch(&mmk_status, 9);
