@@ -115,9 +115,10 @@ __device__ __forceinline__ void node_range(long long n_nodes, long long &n0, lon
     n1 = ((long long)blockIdx.x + 1) * n_nodes / gridDim.x;
 }
 
-// Producer: stream the TMA copies of the CTA's edges [rowptr[n0], rowptr[n1]) in CSR order.  All 32 lanes walk the
-// loop: they fetch the edge ids (and the gathered node of each edge) 32 at a time, one batch ahead, so the index
-// loads overlap the issue of the current batch; lane 0 waits for free stages and issues.  False on a timeout.
+// Producer: stream the TMA copies of the CTA's edges [rowptr[n0], rowptr[n1]) in CSR order.  The warp fetches the
+// edge ids (and the gathered node of each edge) 32 at a time, one batch ahead, so the index loads overlap the issue of
+// the current batch; each lane then waits for its own ring slot and issues its edge's copies, so up to
+// min(32, STAGES) edges are issued at once.  False on a timeout.
 template <int STAGES, class Issue>
 __device__ __forceinline__ bool produce(const int *__restrict__ rowptr, const int *__restrict__ eids,
                                         const long long *__restrict__ other, long long n0, long long n1, u64 *full,
@@ -136,29 +137,35 @@ __device__ __forceinline__ bool produce(const int *__restrict__ rowptr, const in
             e_next = eids[q + 32 + lane];
             o_next = other[e_next];
         }
+        // lanes issue in parallel, in rounds of at most STAGES edges (one ring slot each); lane j of the batch owns
+        // ring position it + j
         const int cnt = min(32, q1 - q);
-        for (int j = 0; j < cnt; ++j, ++it) {
-            const long long ej = __shfl_sync(0xffffffffu, e, j);
-            const long long oj = __shfl_sync(0xffffffffu, o, j);
-            const u32 st = it % STAGES, ph = (it / STAGES) & 1;
+        for (int j0 = 0; j0 < cnt; j0 += STAGES) {
+            const int j = j0 + lane;
+            const long long ej = __shfl_sync(0xffffffffu, e, j & 31);
+            const long long oj = __shfl_sync(0xffffffffu, o, j & 31);
+            const bool mine = lane < STAGES && j < cnt;
+            const u32 i = it + j, st = i % STAGES;
             bool ok = true;
-            if (lane == 0) ok = mbar_wait(&empty[st], ph ^ 1);
-            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return false;
-            if (lane == 0) issue(st, ej, oj, &full[st]);
-            __syncwarp();
+            if (mine) {
+                ok = mbar_wait(&empty[st], ((i / STAGES) & 1) ^ 1);
+                if (ok) issue(st, ej, oj, &full[st]);
+            }
+            if (!__all_sync(0xffffffffu, ok)) {
+                // a slot never came free: let every copy already issued land before the CTA exits
+                if (mine && ok) mbar_wait(&full[st], (i / STAGES) & 1);
+                if (lane == 0) {
+                    const u32 last = it + j0, first = last > STAGES ? last - STAGES : 0;
+                    for (u32 k = first; k < last; ++k) mbar_wait(&full[k % STAGES], (k / STAGES) & 1);
+                }
+                return false;
+            }
         }
+        it += cnt;
     }
     return true;
 }
 
-// After a timeout: wait (bounded) until the copies already issued into the ring have landed, so that no TMA write
-// targets the shared memory of an exited CTA.
-template <int STAGES>
-__device__ __forceinline__ void drain(u64 *full, u32 issued) {
-    if ((threadIdx.x & 31) != 0) return;
-    const u32 first = issued > STAGES ? issued - STAGES : 0;
-    for (u32 i = first; i < issued; ++i) mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
-}
 
 // Consumer groups: the CG groups of MUL threads of a CTA take the edges of a node round-robin (edge j of the node ->
 // group j % CG), so one node's edges are worked on by CG*MUL/32 warps at once; their partial sums are added in shared
@@ -239,10 +246,8 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         };
         long long n0, n1;
         node_range(n_nodes, n0, n1);
-        if (!produce<STAGES>(rowptr, eids, senders, n0, n1, full, empty, it, issue)) {
-            if ((tid & 31) == 0) atomicExch(&mmk_status, 1);
-            drain<STAGES>(full, it);
-        }
+        if (!produce<STAGES>(rowptr, eids, senders, n0, n1, full, empty, it, issue) && (tid & 31) == 0)
+            atomicExch(&mmk_status, 1);
         return;
     }
 
@@ -321,10 +326,8 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         };
         long long n0, n1;
         node_range(n_nodes, n0, n1);
-        if (!produce<STAGES>(rowptr, eids, receivers, n0, n1, full, empty, it, issue)) {
-            if ((tid & 31) == 0) atomicExch(&mmk_status, 3);
-            drain<STAGES>(full, it);
-        }
+        if (!produce<STAGES>(rowptr, eids, receivers, n0, n1, full, empty, it, issue) && (tid & 31) == 0)
+            atomicExch(&mmk_status, 3);
         return;
     }
 

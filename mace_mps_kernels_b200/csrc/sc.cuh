@@ -8,20 +8,25 @@
 // and handed back to the ring around its terms), sc_fwd_store<GG>, sc_load_grad<GG>.
 //
 // Work: nodes are grouped by element (perm / erow: the node CSR of the element index).  A tile is NG*GG nodes of one
-// element.  The CTA has TG consumer groups of CPG threads (CPG = CH*NG rounded up to whole warps) and one producer
-// warp.  Thread (group, sub, c) evaluates channel c of the GG nodes of sub-tile `sub` for the chunks k with
+// element.  The CTA has TG consumer groups of CPG threads (CPG = CH*NG rounded up to whole warps, NG and GG template
+// parameters) and one producer warp.  Thread (group, sub, c) evaluates channel c of the GG nodes of sub-tile `sub` for the chunks k with
 // k % TG == group; every coefficient T[e, row, c] read from shared memory feeds GG nodes.  The producer streams T[e]
 // chunk by chunk (TMA bulk copies of rows*CP contiguous floats) through a STAGES-deep ring of shared memory, each stage
 // released by the warps of the group that owns it.  With TG > 1 the groups' partial sums are added in shared memory
 // in group order (deterministic), handed over with a pair of mbarriers per tile parity.
-// Two instantiations: many nodes -> GG = 4 (bwd 2), TG = 1 (coefficients reused over nodes); few nodes -> GG = 1,
-// TG = 4 (the term list of one node split over four warps per channel group).
+// Two instantiations (GG, NG, TG): many nodes -> one node per thread, NG = 512/CH sub-tiles sharing every staged
+// coefficient row, one group; few nodes -> NG = 128/CH, the term list split over TG = 4 groups.
 // Forward: out[b, off + c*M + m] = sum_t T[e, row_t + m, c] x^idx_t.  Backward: gx[b, c, i] = sum_t (sum_m
 // T[e, row_t + m, c] g[b, off + c*M + m]) d(x^idx_t)/dx_i.  Waits are bounded as in conv_tp.cuh.
 #include "mmk_layer.h"
 
 #define MMK_WAIT_BUDGET (2000000000LL)
-#define CPG (((CH * NG) + 31) / 32 * 32)      // consumer threads per group
+
+// consumer threads per group: CH channels x NG node sub-tiles, rounded up to whole warps
+template <int NG>
+struct Cpg {
+    static constexpr int value = ((CH * NG) + 31) / 32 * 32;
+};
 
 __device__ int mmk_status;
 
@@ -99,8 +104,9 @@ __device__ __forceinline__ Smem smem_layout(float *base) {
     return s;
 }
 
-template <int TG>
+template <int NG, int TG>
 __device__ __forceinline__ void sc_setup(const Smem &s) {
+    constexpr int CPG = Cpg<NG>::value;
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&s.full[i], 1);
@@ -168,8 +174,9 @@ __device__ __forceinline__ void sc_produce(const float *__restrict__ T, const in
 
 // Add the groups' partial sums v[GG][K] of one tile into group 0 (fixed group order).  The buffer half used by
 // tile_it is refilled two tiles later only after group 0 has released it (red_free).  False on a timeout.
-template <int GG, int TG, int K>
+template <int GG, int NG, int TG, int K>
 __device__ __forceinline__ bool reduce_groups(const Smem &s, int grp, int r, u32 tile_it, float (&v)[GG][K]) {
+    constexpr int CPG = Cpg<NG>::value;
     if constexpr (TG == 1) {
         return true;
     } else {
@@ -202,13 +209,14 @@ __device__ __forceinline__ bool reduce_groups(const Smem &s, int grp, int r, u32
     }
 }
 
-template <int GG, int TG>
-__global__ void __launch_bounds__(TG * CPG + 32)
+template <int GG, int NG, int TG>
+__global__ void __launch_bounds__(TG * Cpg<NG>::value + 32)
 mmk_sc_fwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, const int *__restrict__ erow, int n_elem,
                   const float *__restrict__ T, float *__restrict__ out, long long n_tiles) {
     extern __shared__ __align__(128) float smem[];
+    constexpr int CPG = Cpg<NG>::value;
     const Smem s = smem_layout(smem);
-    sc_setup<TG>(s);
+    sc_setup<NG, TG>(s);
     const int tid = threadIdx.x;
     if (tid >= TG * CPG) {
         sc_produce<NG * GG>(T, erow, n_elem, n_tiles, s);
@@ -237,7 +245,7 @@ mmk_sc_fwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, con
             for (int i = 0; i < OUTM; ++i) acc[j][i] = 0.0f;
         }
         if (!sc_fwd_body<GG, TG>(ring, grp, xv, acc)) return;
-        if (!reduce_groups<GG, TG, OUTM>(s, grp, r, tile_it, acc)) {
+        if (!reduce_groups<GG, NG, TG, OUTM>(s, grp, r, tile_it, acc)) {
             if (lane == 0) atomicExch(&mmk_status, 8);
             return;
         }
@@ -245,13 +253,14 @@ mmk_sc_fwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, con
     }
 }
 
-template <int GG, int TG>
-__global__ void __launch_bounds__(TG * CPG + 32)
+template <int GG, int NG, int TG>
+__global__ void __launch_bounds__(TG * Cpg<NG>::value + 32)
 mmk_sc_bwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, const int *__restrict__ erow, int n_elem,
                   const float *__restrict__ T, const float *__restrict__ g, float *__restrict__ gx, long long n_tiles) {
     extern __shared__ __align__(128) float smem[];
+    constexpr int CPG = Cpg<NG>::value;
     const Smem s = smem_layout(smem);
-    sc_setup<TG>(s);
+    sc_setup<NG, TG>(s);
     const int tid = threadIdx.x;
     if (tid >= TG * CPG) {
         sc_produce<NG * GG>(T, erow, n_elem, n_tiles, s);
@@ -281,7 +290,7 @@ mmk_sc_bwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, con
         }
         sc_load_grad<GG>(g, nodes, c, gv);
         if (!sc_bwd_body<GG, TG>(ring, grp, xv, gv, d)) return;
-        if (!reduce_groups<GG, TG, NELL>(s, grp, r, tile_it, d)) {
+        if (!reduce_groups<GG, NG, TG, NELL>(s, grp, r, tile_it, d)) {
             if (lane == 0) atomicExch(&mmk_status, 8);
             return;
         }
