@@ -174,7 +174,7 @@ def conv_case(mod, x, Y, W, ei, name):
                             P(gW), N, E, st)
     bf, bb = conv_bytes(mod.spec, N, E)
     return dict(op=name, kind='conv', N=N, E=E, nnz=mod.spec.nnz, fwd=fwd, bwd=bwd, fwd_bytes=bf, bwd_bytes=bb,
-                keep=(o, g, gx, gY, gW, rr, re_, sr, se))
+                keep=(mod, o, g, gx, gY, gW, rr, re_, sr, se))
 
 
 def sc_case(mod, x, attrs, name):
@@ -192,7 +192,7 @@ def sc_case(mod, x, attrs, name):
     ff, fb = mod.spec.flops()
     C = mod.spec.C
     return dict(op=name, kind='sc', N=N, terms=mod.spec.n_terms, fwd=fwd, bwd=bwd, fwd_flops=ff * N * C,
-                bwd_flops=fb * N * C, keep=(o, g, gx, erow, perm))
+                bwd_flops=fb * N * C, keep=(mod, o, g, gx, erow, perm))
 
 
 def time_cases(cases, reps, flush):

@@ -34,6 +34,22 @@
 // Error status of this module's kernels on this device (0 = ok); read and reset by mmk_conv_layer_status().
 __device__ int mmk_status;
 
+// With MMK_CHECKS defined (environment MMK_CHECKS=1 at layer creation) every gathered index is range-checked: a bad
+// one is recorded in mmk_status (100 + where) and replaced by 0, so the access stays in bounds.
+#ifdef MMK_CHECKS
+#define MMK_CHECK_INDEX(v, n, where)                          \
+    do {                                                      \
+        if ((v) < 0 || (v) >= (n)) {                          \
+            atomicExch(&mmk_status, 100 + (where));           \
+            (v) = 0;                                          \
+        }                                                     \
+    } while (0)
+#else
+#define MMK_CHECK_INDEX(v, n, where) \
+    do {                             \
+    } while (0)
+#endif
+
 typedef unsigned long long u64;
 typedef unsigned int u32;
 
@@ -121,21 +137,26 @@ __device__ __forceinline__ void node_range(long long n_nodes, long long &n0, lon
 // min(32, STAGES) edges are issued at once.  False on a timeout.
 template <int STAGES, class Issue>
 __device__ __forceinline__ bool produce(const int *__restrict__ rowptr, const int *__restrict__ eids,
-                                        const long long *__restrict__ other, long long n0, long long n1, u64 *full,
-                                        u64 *empty, u32 &it, Issue issue) {
+                                        const long long *__restrict__ other, long long n0, long long n1,
+                                        long long n_nodes, long long n_edges, u64 *full, u64 *empty, u32 &it,
+                                        Issue issue) {
     const int lane = threadIdx.x & 31;
     if (n0 >= n1) return true;
     const int q0 = rowptr[n0], q1 = rowptr[n1];
     long long e_next = 0, o_next = 0;
     if (q0 + lane < q1) {
         e_next = eids[q0 + lane];
+        MMK_CHECK_INDEX(e_next, n_edges, 1);
         o_next = other[e_next];
+        MMK_CHECK_INDEX(o_next, n_nodes, 2);
     }
     for (int q = q0; q < q1; q += 32) {
         const long long e = e_next, o = o_next;
         if (q + 32 + lane < q1) {                  // next batch: in flight while this one is issued
             e_next = eids[q + 32 + lane];
+            MMK_CHECK_INDEX(e_next, n_edges, 1);
             o_next = other[e_next];
+            MMK_CHECK_INDEX(o_next, n_nodes, 2);
         }
         // lanes issue in parallel, in rounds of at most STAGES edges (one ring slot each); lane j of the batch owns
         // ring position it + j
@@ -223,7 +244,8 @@ template <int STAGES, int CG>
 __global__ void __launch_bounds__(CG * MUL + 32)
 mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const int *__restrict__ rowptr, const int *__restrict__ eids,
-                    const long long *__restrict__ senders, float *__restrict__ out, long long n_nodes) {
+                    const long long *__restrict__ senders, float *__restrict__ out, long long n_nodes,
+                    long long n_edges) {
     constexpr u32 STAGE_F = W_DIM + X_DIM + 20;     // floats per stage: W row | x row | Y row (16) | edge id (4)
     extern __shared__ __align__(128) float smem[];
     u64 *full = reinterpret_cast<u64 *>(smem + STAGES * STAGE_F);
@@ -246,7 +268,8 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         };
         long long n0, n1;
         node_range(n_nodes, n0, n1);
-        if (!produce<STAGES>(rowptr, eids, senders, n0, n1, full, empty, it, issue) && (tid & 31) == 0)
+        if (!produce<STAGES>(rowptr, eids, senders, n0, n1, n_nodes, n_edges, full, empty, it, issue) &&
+            (tid & 31) == 0)
             atomicExch(&mmk_status, 1);
         return;
     }
@@ -300,7 +323,7 @@ __global__ void __launch_bounds__(CG * MUL + 32)
 mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const float *__restrict__ g, const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ receivers, float *__restrict__ gx, float *__restrict__ gY,
-                    float *__restrict__ gW, long long n_nodes) {
+                    float *__restrict__ gW, long long n_nodes, long long n_edges) {
     constexpr u32 STAGE_F = W_DIM + OUT_DIM + 20;   // W row | grad_out row | Y row (16) | edge id (4)
     extern __shared__ __align__(128) float smem[];
     u64 *full = reinterpret_cast<u64 *>(smem + STAGES * STAGE_F);
@@ -326,7 +349,8 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         };
         long long n0, n1;
         node_range(n_nodes, n0, n1);
-        if (!produce<STAGES>(rowptr, eids, receivers, n0, n1, full, empty, it, issue) && (tid & 31) == 0)
+        if (!produce<STAGES>(rowptr, eids, receivers, n0, n1, n_nodes, n_edges, full, empty, it, issue) &&
+            (tid & 31) == 0)
             atomicExch(&mmk_status, 3);
         return;
     }
@@ -349,7 +373,8 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
                 return;
             }
             const float *stage = smem + st * STAGE_F;
-            const long long e = *reinterpret_cast<const long long *>(stage + W_DIM + OUT_DIM + 16);
+            long long e = *reinterpret_cast<const long long *>(stage + W_DIM + OUT_DIM + 16);
+            MMK_CHECK_INDEX(e, n_edges, 3);
             float y[YD], w[NINS], go[ORR], gw[NINS], gy[16];
 #pragma unroll
             for (int k = 0; k < NINS; ++k) w[k] = stage[k * MUL + u];

@@ -30,6 +30,14 @@ struct Cpg {
 
 __device__ int mmk_status;
 
+// With MMK_CHECKS defined (environment MMK_CHECKS=1 at layer creation) node and element indices are range-checked: a
+// bad one is recorded in mmk_status (100 + where) and the node is skipped.
+#ifdef MMK_CHECKS
+#define MMK_BAD_INDEX(v, n, where) (((v) < 0 || (v) >= (n)) ? (atomicExch(&mmk_status, 100 + (where)), true) : false)
+#else
+#define MMK_BAD_INDEX(v, n, where) false
+#endif
+
 typedef unsigned long long u64;
 typedef unsigned int u32;
 
@@ -212,7 +220,7 @@ __device__ __forceinline__ bool reduce_groups(const Smem &s, int grp, int r, u32
 template <int GG, int NG, int TG>
 __global__ void __launch_bounds__(TG * Cpg<NG>::value + 32)
 mmk_sc_fwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, const int *__restrict__ erow, int n_elem,
-                  const float *__restrict__ T, float *__restrict__ out, long long n_tiles) {
+                  const float *__restrict__ T, float *__restrict__ out, long long n_tiles, long long n_nodes) {
     extern __shared__ __align__(128) float smem[];
     constexpr int CPG = Cpg<NG>::value;
     const Smem s = smem_layout(smem);
@@ -235,6 +243,7 @@ mmk_sc_fwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, con
         for (int j = 0; j < GG; ++j) {
             const int q = sub * GG + j;
             nodes[j] = (sub < NG && q < cnt) ? (long long)perm[p0 + q] : -1;
+            if (nodes[j] >= 0 && MMK_BAD_INDEX(nodes[j], n_nodes, 11)) nodes[j] = -1;
             if (nodes[j] >= 0) {
                 load_feat(x + (nodes[j] * CH + c) * NELL, xv[j]);
             } else {
@@ -256,7 +265,8 @@ mmk_sc_fwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, con
 template <int GG, int NG, int TG>
 __global__ void __launch_bounds__(TG * Cpg<NG>::value + 32)
 mmk_sc_bwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, const int *__restrict__ erow, int n_elem,
-                  const float *__restrict__ T, const float *__restrict__ g, float *__restrict__ gx, long long n_tiles) {
+                  const float *__restrict__ T, const float *__restrict__ g, float *__restrict__ gx, long long n_tiles,
+                  long long n_nodes) {
     extern __shared__ __align__(128) float smem[];
     constexpr int CPG = Cpg<NG>::value;
     const Smem s = smem_layout(smem);
@@ -279,6 +289,7 @@ mmk_sc_bwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, con
         for (int j = 0; j < GG; ++j) {
             const int q = sub * GG + j;
             nodes[j] = (sub < NG && q < cnt) ? (long long)perm[p0 + q] : -1;
+            if (nodes[j] >= 0 && MMK_BAD_INDEX(nodes[j], n_nodes, 11)) nodes[j] = -1;
             if (nodes[j] >= 0) {
                 load_feat(x + (nodes[j] * CH + c) * NELL, xv[j]);
             } else {
