@@ -200,6 +200,7 @@ def time_cases(cases, reps, flush):
     the launch before the GPU reaches the start event; 'hot' = reps launches back to back between two events."""
     res = []
     for c in cases:
+        print(f'[bench] timing {c["op"]}', file=sys.stderr, flush=True)
         out = {k: v for k, v in c.items() if k not in ('fwd', 'bwd', 'keep')}
         for tag in ('fwd', 'bwd'):
             fn = c[tag]

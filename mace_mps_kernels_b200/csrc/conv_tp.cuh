@@ -9,9 +9,9 @@
 //   * one producer warp streams, edge by edge in CSR order, the rows an edge needs into a STAGES-deep ring of shared
 //     memory with TMA bulk copies (cp.async.bulk, completion counted on a per-stage mbarrier): W[e] (NINS*MUL floats)
 //     plus x[sender] (forward) or grad_out[receiver] (backward), plus Y[e] when its row is 16-byte sized;
-//   * CG consumer groups of MUL threads (one per channel u) take a node's edges round-robin: each waits for its
-//     edge's stage, runs the generated per-edge body on its channel's values and releases the stage to the producer;
-//     the groups' partial sums of a node are added in shared memory in group order.
+//   * CG consumer groups of MUL threads (one per channel u) take the edges round-robin: each waits for its edge's
+//     stage, runs the generated per-edge body on its channel's values and releases the stage to the producer; the
+//     groups' partial sums of a node are added in shared memory in group order.
 // Each CTA owns a contiguous range of nodes (a compact domain when atoms are ordered along a space-filling curve), so
 // consecutive nodes gather mostly the same neighbour rows (L2 hits) and the CTA's edges form one stretch of the CSR.
 //   forward   node = receiver; out[n] accumulated in registers over the receiver CSR segment, written once:
@@ -188,9 +188,11 @@ __device__ __forceinline__ bool produce(const int *__restrict__ rowptr, const in
 }
 
 
-// Consumer groups: the CG groups of MUL threads of a CTA take the edges of a node round-robin (edge j of the node ->
-// group j % CG), so one node's edges are worked on by CG*MUL/32 warps at once; their partial sums are added in shared
-// memory in group order (deterministic).  The hand-over buffer has two halves (node parity); red_full[h] completes
+// Consumer groups: the CG groups of MUL threads of a CTA take the CTA's edge stream round-robin (ring position it ->
+// group it % CG), so one node's edges are worked on by CG*MUL/32 warps at once; their partial sums of a node are added
+// in shared memory in group order (deterministic).  STAGES is a multiple of CG, so every ring slot always belongs to
+// the same group: a group only ever waits for the next phase of its own slots, never for a phase of a slot another
+// group has not released yet (an mbarrier parity wait cannot tell phases two apart).  The hand-over buffer has two halves (node parity); red_full[h] completes
 // when groups 1.. have written half h, red_free[h] when group 0 has read it.
 template <int CG, int K>
 __device__ __forceinline__ bool reduce_groups(u64 *red_full, u64 *red_free, float *red, int grp, int u, u32 node_it,
@@ -284,7 +286,7 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         for (int i = 0; i < ORR; ++i) acc[i] = 0.0f;
         const int p0 = rowptr[n], p1 = rowptr[n + 1];
         for (int p = p0; p < p1; ++p, ++it) {
-            if ((p - p0) % CG != grp) continue;
+            if (it % CG != (u32)grp) continue;      // ring position it is always group it % CG's (STAGES % CG == 0)
             const u32 st = it % STAGES, ph = (it / STAGES) & 1;
             if (!mbar_wait(&full[st], ph)) {
                 if (lane == 0) atomicExch(&mmk_status, 2);
@@ -366,7 +368,7 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         for (int i = 0; i < XR; ++i) gxa[i] = 0.0f;
         const int p0 = rowptr[s], p1 = rowptr[s + 1];
         for (int p = p0; p < p1; ++p, ++it) {
-            if ((p - p0) % CG != grp) continue;
+            if (it % CG != (u32)grp) continue;      // ring position it is always group it % CG's (STAGES % CG == 0)
             const u32 st = it % STAGES, ph = (it / STAGES) & 1;
             if (!mbar_wait(&full[st], ph)) {
                 if (lane == 0) atomicExch(&mmk_status, 4);

@@ -4,13 +4,13 @@
 // (reference src/mace_mps_kernels/symmetric.py:52-75 builds the same list): sizes CH (channels), CP (channel stride of
 // the coefficient table, CH rounded up to 4), NELL, NROWS, OUTD (output row), OUTM (outputs per channel), the row
 // chunking of the table (NCHUNK chunks of at most RCH rows cut at term boundaries, CHUNK_ROW0[]), and per chunk the
-// straight-line term code sc_fwd_body<GG, TG> / sc_bwd_body<GG, TG> (chunk k guarded by k % TG == group, taken from
-// and handed back to the ring around its terms), sc_fwd_store<GG>, sc_load_grad<GG>.
+// straight-line term code sc_fwd_body<GG, TG> / sc_bwd_body<GG, TG> (chunk k run by the group that owns its ring
+// position, taken from and handed back to the ring around its terms), sc_fwd_store<GG>, sc_load_grad<GG>.
 //
 // Work: nodes are grouped by element (perm / erow: the node CSR of the element index).  A tile is NG*GG nodes of one
 // element.  The CTA has TG consumer groups of CPG threads (CPG = CH*NG rounded up to whole warps, NG and GG template
-// parameters) and one producer warp.  Thread (group, sub, c) evaluates channel c of the GG nodes of sub-tile `sub` for the chunks k with
-// k % TG == group; every coefficient T[e, row, c] read from shared memory feeds GG nodes.  The producer streams T[e]
+// parameters) and one producer warp.  Thread (group, sub, c) evaluates channel c of the GG nodes of sub-tile `sub` for the chunks whose ring
+// position is group modulo TG; every coefficient T[e, row, c] read from shared memory feeds GG nodes.  The producer streams T[e]
 // chunk by chunk (TMA bulk copies of rows*CP contiguous floats) through a STAGES-deep ring of shared memory, each stage
 // released by the warps of the group that owns it.  With TG > 1 the groups' partial sums are added in shared memory
 // in group order (deterministic), handed over with a pair of mbarriers per tile parity.
@@ -147,6 +147,9 @@ struct Ring {
         if ((threadIdx.x & 31) == 0) mbar_arrive(&s.empty[(it + k) % STAGES]);
     }
     __device__ __forceinline__ void advance(int n) { it += n; }
+    // group that consumes chunk k of this tile: by ring position, so that (STAGES a multiple of TG) every slot always
+    // belongs to one group and a group never waits on a phase of a slot another group still holds
+    __device__ __forceinline__ int owner(int k, int tg) const { return (int)((it + k) % (u32)tg); }
 };
 
 template <int TN>

@@ -37,6 +37,9 @@ CONV_CASES = [
     ('96x0e+96x1o', 3, 3, 17),
     ('64x0e+64x1o', 3, 3000, 90000),
     ('32x0e+32x1o', 3, 5, 900),
+    # many nodes per CTA with small rings and two consumer groups (node boundaries inside a CTA's edge stream)
+    ('128x0e+128x1o+128x2e', 3, 2000, 40000),
+    ('128x0e', 3, 4000, 120000),
 ]
 
 
@@ -121,6 +124,9 @@ SC_CASES = [
     ('32x0e+32x1o+32x2e', 3, 3, 25),
     ('128x0e+128x1o', 3, 3, 1001),
     ('32x0e', 2, 3, 3),
+    # few-node variant (term list split over four groups) with several tiles per CTA, and the many-node variant
+    ('128x0e+128x1o+128x2e', 3, 3, 900),
+    ('128x0e+128x1o', 3, 3, 3000),
 ]
 
 
