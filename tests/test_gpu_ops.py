@@ -38,7 +38,7 @@ CONV_CASES = [
     ('64x0e+64x1o', 3, 3000, 90000),
     ('32x0e+32x1o', 3, 5, 900),
     # many nodes per CTA with small rings and two consumer groups (node boundaries inside a CTA's edge stream)
-    ('128x0e+128x1o+128x2e', 3, 2000, 40000),
+    ('128x0e+128x1o+128x2e', 3, 1500, 24000),
     ('128x0e', 3, 4000, 120000),
 ]
 
