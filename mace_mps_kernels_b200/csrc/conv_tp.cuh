@@ -27,7 +27,6 @@
 #define X_DIM (XR * MUL)
 #define OUT_DIM (ORR * MUL)
 #define W_DIM (NINS * MUL)
-#define NCW (MUL / 32)                      // warps of one consumer group
 #define Y_TMA ((YD * 4) % 16 == 0)         // Y rows are copied with TMA when 16-byte sized
 #define MMK_WAIT_BUDGET (2000000000LL)      // clock64 cycles, ~1 s
 
@@ -158,14 +157,16 @@ __device__ __forceinline__ bool produce(const int *__restrict__ rowptr, const in
             o_next = other[e_next];
             MMK_CHECK_INDEX(o_next, n_nodes, 2);
         }
-        // lanes issue in parallel, in rounds of at most STAGES edges (one ring slot each); lane j of the batch owns
-        // ring position it + j
+        // lanes issue in parallel, in rounds of ROUND edges (one ring slot each; lane j of the batch owns ring position
+        // it + j).  A round waits for the slowest of its slots, so ROUND is a fraction of the ring (STAGES / 2 by
+        // default): the slots of the next round are being refilled while the current round is consumed.
+        constexpr int ROUND = STAGES / MMK_ROUND_DIV < 1 ? 1 : (STAGES / MMK_ROUND_DIV > 32 ? 32 : STAGES / MMK_ROUND_DIV);
         const int cnt = min(32, q1 - q);
-        for (int j0 = 0; j0 < cnt; j0 += STAGES) {
+        for (int j0 = 0; j0 < cnt; j0 += ROUND) {
             const int j = j0 + lane;
             const long long ej = __shfl_sync(0xffffffffu, e, j & 31);
             const long long oj = __shfl_sync(0xffffffffu, o, j & 31);
-            const bool mine = lane < STAGES && j < cnt;
+            const bool mine = lane < ROUND && j < cnt;
             const u32 i = it + j, st = i % STAGES;
             bool ok = true;
             if (mine) {
@@ -194,29 +195,34 @@ __device__ __forceinline__ bool produce(const int *__restrict__ rowptr, const in
 // the same group: a group only ever waits for the next phase of its own slots, never for a phase of a slot another
 // group has not released yet (an mbarrier parity wait cannot tell phases two apart).  The hand-over buffer has two halves (node parity); red_full[h] completes
 // when groups 1.. have written half h, red_free[h] when group 0 has read it.
-template <int CG, int K>
-__device__ __forceinline__ bool reduce_groups(u64 *red_full, u64 *red_free, float *red, int grp, int u, u32 node_it,
-                                              float (&v)[K]) {
+template <int CG, int CPT, int K>
+__device__ __forceinline__ bool reduce_groups(u64 *red_full, u64 *red_free, float *red, int grp, int u0, u32 node_it,
+                                              float (&v)[CPT][K]) {
     if constexpr (CG == 1) {
         return true;
     } else {
+        constexpr int GT = MUL / CPT;
         const u32 h = node_it & 1, ph = (node_it >> 1) & 1;
         float *buf = red + (size_t)h * (CG - 1) * K * MUL;
         const int lane = threadIdx.x & 31;
         if (grp > 0) {
             if (!mbar_wait(&red_free[h], ph ^ 1)) return false;
-            float *dst = buf + (size_t)(grp - 1) * K * MUL + u;
+            float *dst = buf + (size_t)(grp - 1) * K * MUL + u0;
 #pragma unroll
-            for (int i = 0; i < K; ++i) dst[i * MUL] = v[i];
+            for (int q = 0; q < CPT; ++q)
+#pragma unroll
+                for (int i = 0; i < K; ++i) dst[i * MUL + q * GT] = v[q][i];
             __syncwarp();
             if (lane == 0) mbar_arrive(&red_full[h]);
         } else {
             if (!mbar_wait(&red_full[h], ph)) return false;
 #pragma unroll
-            for (int q = 0; q < CG - 1; ++q) {
-                const float *src = buf + (size_t)q * K * MUL + u;
+            for (int g = 0; g < CG - 1; ++g) {
+                const float *src = buf + (size_t)g * K * MUL + u0;
 #pragma unroll
-                for (int i = 0; i < K; ++i) v[i] += src[i * MUL];
+                for (int q = 0; q < CPT; ++q)
+#pragma unroll
+                    for (int i = 0; i < K; ++i) v[q][i] += src[i * MUL + q * GT];
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&red_free[h]);
@@ -225,12 +231,27 @@ __device__ __forceinline__ bool reduce_groups(u64 *red_full, u64 *red_free, floa
     }
 }
 
-__device__ __forceinline__ void init_barriers(u64 *full, u64 *empty, int stages, u64 *extra, int n_extra, u32 extra_count,
-                                              u64 *extra2, int n_extra2, u32 extra2_count) {
+// Y[e] of a stage: four 16-byte shared-memory loads (the same address in every lane: broadcast) when the row was
+// copied with TMA, else read from global memory.
+__device__ __forceinline__ void load_y(const float *ys, const float *__restrict__ Y, long long e, float (&y)[YD]) {
+    if constexpr (Y_TMA) {
+#pragma unroll
+        for (int j = 0; j < YD / 4; ++j) {
+            const float4 q = reinterpret_cast<const float4 *>(ys)[j];
+            y[4 * j] = q.x; y[4 * j + 1] = q.y; y[4 * j + 2] = q.z; y[4 * j + 3] = q.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < YD; ++j) y[j] = __ldg(Y + e * YD + j);
+    }
+}
+
+__device__ __forceinline__ void init_barriers(u64 *full, u64 *empty, int stages, u32 ncw, u64 *extra, int n_extra,
+                                              u32 extra_count, u64 *extra2, int n_extra2, u32 extra2_count) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NCW);
+            mbar_init(&empty[s], ncw);
         }
         for (int i = 0; i < n_extra; ++i) mbar_init(&extra[i], extra_count);
         for (int i = 0; i < n_extra2; ++i) mbar_init(&extra2[i], extra2_count);
@@ -242,12 +263,14 @@ __device__ __forceinline__ void init_barriers(u64 *full, u64 *empty, int stages,
 // ------------------------------------------------------------------------------------------------------------------
 // forward
 // ------------------------------------------------------------------------------------------------------------------
-template <int STAGES, int CG>
-__global__ void __launch_bounds__(CG * MUL + 32)
+template <int STAGES, int CG, int CPT>
+__global__ void __launch_bounds__(CG * (MUL / CPT) + 32)
 mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ senders, float *__restrict__ out, long long n_nodes,
                     long long n_edges) {
+    constexpr int GT = MUL / CPT;                   // threads of one consumer group; thread u0 has channels u0 + q*GT
+    constexpr u32 NCW = GT / 32;                    // warps of one consumer group
     constexpr u32 STAGE_F = W_DIM + X_DIM + 20;     // floats per stage: W row | x row | Y row (16) | edge id (4)
     extern __shared__ __align__(128) float smem[];
     u64 *full = reinterpret_cast<u64 *>(smem + STAGES * STAGE_F);
@@ -256,9 +279,9 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     u64 *red_free = red_full + 2;                   // [2]
     float *red = reinterpret_cast<float *>(red_free + 2);   // [2][CG-1][ORR][MUL]
     const int tid = threadIdx.x;
-    init_barriers(full, empty, STAGES, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
+    init_barriers(full, empty, STAGES, NCW, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
 
-    if (tid >= CG * MUL) {                          // producer warp
+    if (tid >= CG * GT) {                           // producer warp
         u32 it = 0;
         auto issue = [&](u32 st, long long e, long long s, u64 *bar) {
             float *stage = smem + st * STAGE_F;
@@ -276,14 +299,16 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         return;
     }
 
-    const int grp = tid / MUL, u = tid % MUL, lane = tid & 31;
+    const int grp = tid / GT, u0 = tid % GT, lane = tid & 31;
     u32 it = 0, node_it = 0;
     long long n0, n1;
     node_range(n_nodes, n0, n1);
     for (long long n = n0; n < n1; ++n, ++node_it) {
-        float acc[ORR];
+        float acc[CPT][ORR];
 #pragma unroll
-        for (int i = 0; i < ORR; ++i) acc[i] = 0.0f;
+        for (int q = 0; q < CPT; ++q)
+#pragma unroll
+            for (int i = 0; i < ORR; ++i) acc[q][i] = 0.0f;
         const int p0 = rowptr[n], p1 = rowptr[n + 1];
         for (int p = p0; p < p1; ++p, ++it) {
             if (it % CG != (u32)grp) continue;      // ring position it is always group it % CG's (STAGES % CG == 0)
@@ -293,39 +318,42 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
                 return;
             }
             const float *stage = smem + st * STAGE_F;
-            float xs[XR], y[YD], w[NINS];
+            float xs[CPT][XR], y[YD], w[CPT][NINS];
+            load_y(stage + W_DIM + X_DIM, Y, *reinterpret_cast<const long long *>(stage + W_DIM + X_DIM + 16), y);
 #pragma unroll
-            for (int k = 0; k < NINS; ++k) w[k] = stage[k * MUL + u];
-            load_x_s(stage + W_DIM, u, xs);
-            if constexpr (Y_TMA) {
+            for (int q = 0; q < CPT; ++q) {
+                const int u = u0 + q * GT;
 #pragma unroll
-                for (int j = 0; j < YD; ++j) y[j] = stage[W_DIM + X_DIM + j];
-            } else {
-                const long long e = *reinterpret_cast<const long long *>(stage + W_DIM + X_DIM + 16);
-#pragma unroll
-                for (int j = 0; j < YD; ++j) y[j] = __ldg(Y + e * YD + j);
+                for (int k = 0; k < NINS; ++k) w[q][k] = stage[k * MUL + u];
+                load_x_s(stage + W_DIM, u, xs[q]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
-            fwd_edge(xs, y, w, acc);
+#pragma unroll
+            for (int q = 0; q < CPT; ++q) fwd_edge(xs[q], y, w[q], acc[q]);
         }
-        if (!reduce_groups<CG, ORR>(red_full, red_free, red, grp, u, node_it, acc)) {
+        if (!reduce_groups<CG, CPT, ORR>(red_full, red_free, red, grp, u0, node_it, acc)) {
             if (lane == 0) atomicExch(&mmk_status, 9);
             return;
         }
-        if (grp == 0) store_out(out + n * OUT_DIM, u, acc);
+        if (grp == 0) {
+#pragma unroll
+            for (int q = 0; q < CPT; ++q) store_out(out + n * OUT_DIM, u0 + q * GT, acc[q]);
+        }
     }
 }
 
 // ------------------------------------------------------------------------------------------------------------------
 // backward
 // ------------------------------------------------------------------------------------------------------------------
-template <int STAGES, int CG>
-__global__ void __launch_bounds__(CG * MUL + 32)
+template <int STAGES, int CG, int CPT>
+__global__ void __launch_bounds__(CG * (MUL / CPT) + 32)
 mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const float *__restrict__ g, const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ receivers, float *__restrict__ gx, float *__restrict__ gY,
                     float *__restrict__ gW, long long n_nodes, long long n_edges) {
+    constexpr int GT = MUL / CPT;                   // threads of one consumer group; thread u0 has channels u0 + q*GT
+    constexpr u32 NCW = GT / 32;                    // warps of one consumer group
     constexpr u32 STAGE_F = W_DIM + OUT_DIM + 20;   // W row | grad_out row | Y row (16) | edge id (4)
     extern __shared__ __align__(128) float smem[];
     u64 *full = reinterpret_cast<u64 *>(smem + STAGES * STAGE_F);
@@ -337,9 +365,9 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     float *red = reinterpret_cast<float *>(arrived + STAGES);    // [2][CG-1][XR][MUL]
     const int tid = threadIdx.x;
     for (int i = tid; i < STAGES; i += blockDim.x) arrived[i] = 0;
-    init_barriers(full, empty, STAGES, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
+    init_barriers(full, empty, STAGES, NCW, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
 
-    if (tid >= CG * MUL) {
+    if (tid >= CG * GT) {
         u32 it = 0;
         auto issue = [&](u32 st, long long e, long long r, u64 *bar) {
             float *stage = smem + st * STAGE_F;
@@ -357,15 +385,18 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         return;
     }
 
-    const int grp = tid / MUL, u = tid % MUL, warp = u >> 5, lane = tid & 31;
+    const int grp = tid / GT, u0 = tid % GT, warp = u0 >> 5, lane = tid & 31;
     u32 it = 0, node_it = 0;
     long long n0, n1;
     node_range(n_nodes, n0, n1);
     for (long long s = n0; s < n1; ++s, ++node_it) {
-        float xs[XR], gxa[XR];
-        load_x(x + s * X_DIM, u, xs);
+        float xs[CPT][XR], gxa[CPT][XR];
 #pragma unroll
-        for (int i = 0; i < XR; ++i) gxa[i] = 0.0f;
+        for (int q = 0; q < CPT; ++q) {
+            load_x(x + s * X_DIM, u0 + q * GT, xs[q]);
+#pragma unroll
+            for (int i = 0; i < XR; ++i) gxa[q][i] = 0.0f;
+        }
         const int p0 = rowptr[s], p1 = rowptr[s + 1];
         for (int p = p0; p < p1; ++p, ++it) {
             if (it % CG != (u32)grp) continue;      // ring position it is always group it % CG's (STAGES % CG == 0)
@@ -377,27 +408,26 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
             const float *stage = smem + st * STAGE_F;
             long long e = *reinterpret_cast<const long long *>(stage + W_DIM + OUT_DIM + 16);
             MMK_CHECK_INDEX(e, n_edges, 3);
-            float y[YD], w[NINS], go[ORR], gw[NINS], gy[16];
-#pragma unroll
-            for (int k = 0; k < NINS; ++k) w[k] = stage[k * MUL + u];
-            load_out_s(stage + W_DIM, u, go);
-            if constexpr (Y_TMA) {
-#pragma unroll
-                for (int j = 0; j < YD; ++j) y[j] = stage[W_DIM + OUT_DIM + j];
-            } else {
-#pragma unroll
-                for (int j = 0; j < YD; ++j) y[j] = __ldg(Y + e * YD + j);
-            }
+            float y[YD], gy[16];
+            load_y(stage + W_DIM + OUT_DIM, Y, e, y);
 #pragma unroll
             for (int j = 0; j < 16; ++j) gy[j] = 0.0f;
-            bwd_edge(xs, y, w, go, gxa, gw, gy);
-            if (gW != nullptr) {
-                float *gwe = gW + e * W_DIM + u;
 #pragma unroll
-                for (int k = 0; k < NINS; ++k) gwe[k * MUL] = gw[k];
+            for (int q = 0; q < CPT; ++q) {
+                const int u = u0 + q * GT;
+                float w[NINS], go[ORR], gw[NINS];
+#pragma unroll
+                for (int k = 0; k < NINS; ++k) w[k] = stage[k * MUL + u];
+                load_out_s(stage + W_DIM, u, go);
+                bwd_edge(xs[q], y, w, go, gxa[q], gw, gy);
+                if (gW != nullptr) {
+                    float *gwe = gW + e * W_DIM + u;
+#pragma unroll
+                    for (int k = 0; k < NINS; ++k) gwe[k * MUL] = gw[k];
+                }
             }
             if (gY != nullptr) {
-                // channel sum of gY[e]: each warp reduces its 32 channels in registers and leaves 16 partials in the
+                // channel sum of gY[e]: each warp reduces its channels in registers and leaves 16 partials in the
                 // stage's slot; the warp that finishes last adds the NCW partials in warp order (deterministic),
                 // writes gY[e] and clears the counter.  The stage is released only afterwards, so the slot is free.
                 float *pb = part + (size_t)st * NCW * 16;
@@ -407,14 +437,14 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
                 int last = 0;
                 if (lane == 0) {
                     __threadfence_block();
-                    last = atomicAdd(&arrived[st], 1) == NCW - 1;
+                    last = atomicAdd(&arrived[st], 1) == (int)NCW - 1;
                     if (last) __threadfence_block();
                 }
                 if (__shfl_sync(0xffffffffu, last, 0)) {
                     if (lane < YD) {
                         float t = 0.0f;
 #pragma unroll
-                        for (int q = 0; q < NCW; ++q) t += pb[q * 16 + lane];
+                        for (int w8 = 0; w8 < (int)NCW; ++w8) t += pb[w8 * 16 + lane];
                         gY[e * YD + lane] = t;
                     }
                     if (lane == 0) arrived[st] = 0;
@@ -423,10 +453,13 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
         }
-        if (!reduce_groups<CG, XR>(red_full, red_free, red, grp, u, node_it, gxa)) {
+        if (!reduce_groups<CG, CPT, XR>(red_full, red_free, red, grp, u0, node_it, gxa)) {
             if (lane == 0) atomicExch(&mmk_status, 9);
             return;
         }
-        if (gx != nullptr && grp == 0) store_x(gx + s * X_DIM, u, gxa);
+        if (gx != nullptr && grp == 0) {
+#pragma unroll
+            for (int q = 0; q < CPT; ++q) store_x(gx + s * X_DIM, u0 + q * GT, gxa[q]);
+        }
     }
 }

@@ -45,6 +45,28 @@ CONV_CASES = [
 
 @pytest.mark.parametrize('hidden,lmax,N,E', CONV_CASES)
 def test_conv_fwd_bwd_matches_oracle(cuda, hidden, lmax, N, E):
+    _conv_case(cuda, hidden, lmax, N, E)
+
+
+# Alternative launch plans (the layer-creation overrides used for tuning): channels per consumer thread, group
+# counts, ring sizes and the per-term backward body.
+PLAN_VARIANTS = [
+    {'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2'},
+    {'MMK_CONV_FWD_CPT': '4', 'MMK_CONV_BWD_CPT': '4', 'MMK_CONV_FWD_CG': '8', 'MMK_CONV_BWD_CG': '8'},
+    {'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2', 'MMK_CONV_FWD_CG': '8', 'MMK_CONV_BWD_CG': '8'},
+    {'MMK_CONV_BWD_FORM': '0', 'MMK_CONV_SMEM_KB': '220', 'MMK_CONV_FWD_CG': '1', 'MMK_CONV_BWD_CG': '1'},
+]
+
+
+@pytest.mark.parametrize('env', PLAN_VARIANTS, ids=lambda e: ','.join(f'{k[9:]}={v}' for k, v in e.items()))
+@pytest.mark.parametrize('hidden,N,E', [('128x0e', 1500, 30000), ('128x0e+128x1o', 300, 6000)])
+def test_conv_plan_variants_match_oracle(cuda, monkeypatch, env, hidden, N, E):
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    _conv_case(cuda, hidden, 3, N, E)
+
+
+def _conv_case(cuda, hidden, lmax, N, E):
     from mace_mps_kernels_b200.conv import CudaConvTP
     torch.manual_seed(0)
     tp = helpers.conv_tp(hidden, lmax).to(cuda)
