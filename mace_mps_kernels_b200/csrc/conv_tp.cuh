@@ -28,6 +28,18 @@
 #define OUT_DIM (ORR * MUL)
 #define W_DIM (NINS * MUL)
 #define Y_TMA ((YD * 4) % 16 == 0)         // Y rows are copied with TMA when 16-byte sized
+// launch bounds: the block size, plus a minimum of resident CTAs per SM when the plan asks for one (MMK_*_MINB > 0;
+// it caps the registers per thread), else the register count is left to the compiler
+#if MMK_FWD_MINB > 0
+#define MMK_FWD_BOUNDS(T) __launch_bounds__(T, MMK_FWD_MINB)
+#else
+#define MMK_FWD_BOUNDS(T) __launch_bounds__(T)
+#endif
+#if MMK_BWD_MINB > 0
+#define MMK_BWD_BOUNDS(T) __launch_bounds__(T, MMK_BWD_MINB)
+#else
+#define MMK_BWD_BOUNDS(T) __launch_bounds__(T)
+#endif
 #define MMK_WAIT_BUDGET (2000000000LL)      // clock64 cycles, ~1 s
 
 // Error status of this module's kernels on this device (0 = ok); read and reset by mmk_conv_layer_status().
@@ -263,14 +275,68 @@ __device__ __forceinline__ void init_barriers(u64 *full, u64 *empty, int stages,
 // ------------------------------------------------------------------------------------------------------------------
 // forward
 // ------------------------------------------------------------------------------------------------------------------
-template <int STAGES, int CG, int CPT>
-__global__ void __launch_bounds__(CG * (MUL / CPT) + 32)
+// Consumer code of part H of a group (the forward's per-thread work; see mmk_conv_fwd_kernel).
+template <int STAGES, int CG, int CPT, int NP, int H>
+__device__ __forceinline__ void fwd_consume(const float *smem, u64 *full, u64 *empty, u64 *red_full, u64 *red_free,
+                                            float *red, const float *__restrict__ Y, const int *__restrict__ rowptr,
+                                            float *__restrict__ out, long long n_nodes, int grp, int u0, int lane) {
+    constexpr int GT = MUL / CPT;
+    constexpr u32 STAGE_F = W_DIM + X_DIM + 20;
+    u32 it = 0, node_it = 0;
+    long long n0, n1;
+    node_range(n_nodes, n0, n1);
+    for (long long n = n0; n < n1; ++n, ++node_it) {
+        float acc[CPT][ORR];
+#pragma unroll
+        for (int q = 0; q < CPT; ++q)
+#pragma unroll
+            for (int i = 0; i < ORR; ++i) acc[q][i] = 0.0f;
+        const int p0 = rowptr[n], p1 = rowptr[n + 1];
+        for (int p = p0; p < p1; ++p, ++it) {
+            if (it % CG != (u32)grp) continue;  // ring position it is always group it % CG's (STAGES % CG == 0)
+            const u32 st = it % STAGES, ph = (it / STAGES) & 1;
+            if (!mbar_wait(&full[st], ph)) {
+                if (lane == 0) atomicExch(&mmk_status, 2);
+                return;
+            }
+            const float *stage = smem + st * STAGE_F;
+            float xs[CPT][XR], y[YD], w[CPT][NINS];
+            load_y(stage + W_DIM + X_DIM, Y, *reinterpret_cast<const long long *>(stage + W_DIM + X_DIM + 16), y);
+#pragma unroll
+            for (int q = 0; q < CPT; ++q) {
+                const int u = u0 + q * GT;
+                fwd_load_w<H>(stage, u, w[q]);
+                load_x_s(stage + W_DIM, u, xs[q]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+#pragma unroll
+            for (int q = 0; q < CPT; ++q) fwd_edge<H>(xs[q], y, w[q], acc[q]);
+        }
+        if (!reduce_groups<CG, CPT, ORR>(red_full, red_free, red, grp, u0, node_it, acc)) {
+            if (lane == 0) atomicExch(&mmk_status, 9);
+            return;
+        }
+        if (grp == 0) {
+#pragma unroll
+            for (int q = 0; q < CPT; ++q) fwd_store<H>(out + n * OUT_DIM, u0 + q * GT, acc[q]);
+        }
+    }
+}
+
+// CTA = CG consumer groups x NP parts x GT = MUL / CPT threads (+ the producer warp).  Thread (grp, part, u0) computes,
+// for channels u0 + q*GT (q < CPT), the outputs of part `part` of the instructions; every part of a group reads every
+// stage the group owns.  With NP > 1 the plan runs one group (no cross-group sum of the outputs).
+template <int STAGES, int CG, int CPT, int NP>
+__global__ void MMK_FWD_BOUNDS(CG * NP * (MUL / CPT) + 32)
 mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ senders, float *__restrict__ out, long long n_nodes,
                     long long n_edges) {
-    constexpr int GT = MUL / CPT;                   // threads of one consumer group; thread u0 has channels u0 + q*GT
-    constexpr u32 NCW = GT / 32;                    // warps of one consumer group
+    static_assert(NP == 1 || CG == 1, "a forward split over parts runs one consumer group");
+    constexpr int GT = MUL / CPT;                   // threads of one part of a group
+    constexpr u32 NCW = GT / 32;                    // warps of one part
+    constexpr int GTH = NP * GT;                    // threads of one group
     constexpr u32 STAGE_F = W_DIM + X_DIM + 20;     // floats per stage: W row | x row | Y row (16) | edge id (4)
     extern __shared__ __align__(128) float smem[];
     u64 *full = reinterpret_cast<u64 *>(smem + STAGES * STAGE_F);
@@ -279,9 +345,9 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     u64 *red_free = red_full + 2;                   // [2]
     float *red = reinterpret_cast<float *>(red_free + 2);   // [2][CG-1][ORR][MUL]
     const int tid = threadIdx.x;
-    init_barriers(full, empty, STAGES, NCW, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
+    init_barriers(full, empty, STAGES, NP * NCW, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
 
-    if (tid >= CG * GT) {                           // producer warp
+    if (tid >= CG * GTH) {                          // producer warp
         u32 it = 0;
         auto issue = [&](u32 st, long long e, long long s, u64 *bar) {
             float *stage = smem + st * STAGE_F;
@@ -299,75 +365,131 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         return;
     }
 
-    const int grp = tid / GT, u0 = tid % GT, lane = tid & 31;
-    u32 it = 0, node_it = 0;
-    long long n0, n1;
-    node_range(n_nodes, n0, n1);
-    for (long long n = n0; n < n1; ++n, ++node_it) {
-        float acc[CPT][ORR];
-#pragma unroll
-        for (int q = 0; q < CPT; ++q)
-#pragma unroll
-            for (int i = 0; i < ORR; ++i) acc[q][i] = 0.0f;
-        const int p0 = rowptr[n], p1 = rowptr[n + 1];
-        for (int p = p0; p < p1; ++p, ++it) {
-            if (it % CG != (u32)grp) continue;      // ring position it is always group it % CG's (STAGES % CG == 0)
-            const u32 st = it % STAGES, ph = (it / STAGES) & 1;
-            if (!mbar_wait(&full[st], ph)) {
-                if (lane == 0) atomicExch(&mmk_status, 2);
-                return;
-            }
-            const float *stage = smem + st * STAGE_F;
-            float xs[CPT][XR], y[YD], w[CPT][NINS];
-            load_y(stage + W_DIM + X_DIM, Y, *reinterpret_cast<const long long *>(stage + W_DIM + X_DIM + 16), y);
-#pragma unroll
-            for (int q = 0; q < CPT; ++q) {
-                const int u = u0 + q * GT;
-#pragma unroll
-                for (int k = 0; k < NINS; ++k) w[q][k] = stage[k * MUL + u];
-                load_x_s(stage + W_DIM, u, xs[q]);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
-#pragma unroll
-            for (int q = 0; q < CPT; ++q) fwd_edge(xs[q], y, w[q], acc[q]);
-        }
-        if (!reduce_groups<CG, CPT, ORR>(red_full, red_free, red, grp, u0, node_it, acc)) {
-            if (lane == 0) atomicExch(&mmk_status, 9);
-            return;
-        }
-        if (grp == 0) {
-#pragma unroll
-            for (int q = 0; q < CPT; ++q) store_out(out + n * OUT_DIM, u0 + q * GT, acc[q]);
-        }
+    const int grp = tid / GTH, part = (tid % GTH) / GT, u0 = tid % GT, lane = tid & 31;
+    if (part == 0) fwd_consume<STAGES, CG, CPT, NP, 0>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, grp, u0, lane);
+    if constexpr (NP > 1) {
+        if (part == 1) fwd_consume<STAGES, CG, CPT, NP, 1>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, grp, u0, lane);
+    }
+    if constexpr (NP > 2) {
+        if (part == 2) fwd_consume<STAGES, CG, CPT, NP, 2>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, grp, u0, lane);
+        if (part == 3) fwd_consume<STAGES, CG, CPT, NP, 3>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, grp, u0, lane);
     }
 }
 
 // ------------------------------------------------------------------------------------------------------------------
 // backward
 // ------------------------------------------------------------------------------------------------------------------
-template <int STAGES, int CG, int CPT>
-__global__ void __launch_bounds__(CG * (MUL / CPT) + 32)
+// Consumer code of part H of a group (the backward's per-thread work; see mmk_conv_bwd_kernel).
+template <int STAGES, int CG, int CPT, int NP, int H>
+__device__ __forceinline__ void bwd_consume(const float *smem, u64 *full, u64 *empty, u64 *red_full, u64 *red_free,
+                                            float *red, float *part_buf, int *arrived, const float *__restrict__ x,
+                                            const float *__restrict__ Y, const int *__restrict__ rowptr,
+                                            float *__restrict__ gx, float *__restrict__ gY, float *__restrict__ gW,
+                                            long long n_nodes, long long n_edges, int grp, int lg, int u0, int gwarp,
+                                            int lane) {
+    constexpr int GT = MUL / CPT;
+    constexpr u32 GW = NP * (GT / 32);
+    constexpr u32 STAGE_F = W_DIM + OUT_DIM + 20;
+    u32 it = 0, node_it = 0;
+    long long n0, n1;
+    node_range(n_nodes, n0, n1);
+    for (long long s = n0; s < n1; ++s, ++node_it) {
+        float xs[CPT][XR], gxa[CPT][XR];
+#pragma unroll
+        for (int q = 0; q < CPT; ++q) {
+            load_x(x + s * X_DIM, u0 + q * GT, xs[q]);
+#pragma unroll
+            for (int i = 0; i < XR; ++i) gxa[q][i] = 0.0f;
+        }
+        const int p0 = rowptr[s], p1 = rowptr[s + 1];
+        for (int p = p0; p < p1; ++p, ++it) {
+            if (it % CG != (u32)grp) continue;  // ring position it is always group it % CG's (STAGES % CG == 0)
+            const u32 st = it % STAGES, ph = (it / STAGES) & 1;
+            if (!mbar_wait(&full[st], ph)) {
+                if (lane == 0) atomicExch(&mmk_status, 4);
+                return;
+            }
+            const float *stage = smem + st * STAGE_F;
+            long long e = *reinterpret_cast<const long long *>(stage + W_DIM + OUT_DIM + 16);
+            MMK_CHECK_INDEX(e, n_edges, 3);
+            float y[YD], gy[16];
+            load_y(stage + W_DIM + OUT_DIM, Y, e, y);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) gy[j] = 0.0f;
+#pragma unroll
+            for (int q = 0; q < CPT; ++q) {
+                const int u = u0 + q * GT;
+                float w[NINS], go[ORR], gw[NINS];
+                bwd_load_w<H>(stage, u, w);
+                bwd_load_g<H>(stage + W_DIM, u, go);
+                bwd_edge<H>(xs[q], y, w, go, gxa[q], gw, gy);
+                if (gW != nullptr) bwd_store_gw<H>(gW + e * W_DIM + u, gw);
+            }
+            if (gY != nullptr) {
+                // channel sum of gY[e]: each warp reduces its channels in registers and leaves 16 partials in the
+                // stage's slot; the warp that finishes last adds the GW partials in warp order (deterministic),
+                // writes gY[e] and clears the counter.  The stage is released only afterwards, so the slot is
+                // free.
+                float *pb = part_buf + (size_t)st * GW * 16;
+                const float v = warp_transpose_reduce16(gy);
+                if ((lane & 1) == 0) pb[gwarp * 16 + (lane >> 1)] = v;
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) {
+                    __threadfence_block();
+                    last = atomicAdd(&arrived[st], 1) == (int)GW - 1;
+                    if (last) __threadfence_block();
+                }
+                if (__shfl_sync(0xffffffffu, last, 0)) {
+                    if (lane < YD) {
+                        float t = 0.0f;
+#pragma unroll
+                        for (int w8 = 0; w8 < (int)GW; ++w8) t += pb[w8 * 16 + lane];
+                        gY[e * YD + lane] = t;
+                    }
+                    if (lane == 0) arrived[st] = 0;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+        if (!reduce_groups<CG * NP, CPT, XR>(red_full, red_free, red, lg, u0, node_it, gxa)) {
+            if (lane == 0) atomicExch(&mmk_status, 9);
+            return;
+        }
+        if (gx != nullptr && lg == 0) {
+#pragma unroll
+            for (int q = 0; q < CPT; ++q) store_x(gx + s * X_DIM, u0 + q * GT, gxa[q]);
+        }
+    }
+}
+
+// Same CTA shape.  The CG*NP (group, part) pairs are the "logical groups" of the gx sum at the end of a sender: each
+// holds a partial gx[s] (its edges, its instructions), added in shared memory in logical-group order.
+template <int STAGES, int CG, int CPT, int NP>
+__global__ void MMK_BWD_BOUNDS(CG * NP * (MUL / CPT) + 32)
 mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const float *__restrict__ g, const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ receivers, float *__restrict__ gx, float *__restrict__ gY,
                     float *__restrict__ gW, long long n_nodes, long long n_edges) {
-    constexpr int GT = MUL / CPT;                   // threads of one consumer group; thread u0 has channels u0 + q*GT
-    constexpr u32 NCW = GT / 32;                    // warps of one consumer group
+    constexpr int GT = MUL / CPT;                   // threads of one part of a group
+    constexpr u32 NCW = GT / 32;                    // warps of one part
+    constexpr int GTH = NP * GT;                    // threads of one group
+    constexpr u32 GW = NP * NCW;                    // warps of one group
     constexpr u32 STAGE_F = W_DIM + OUT_DIM + 20;   // W row | grad_out row | Y row (16) | edge id (4)
     extern __shared__ __align__(128) float smem[];
     u64 *full = reinterpret_cast<u64 *>(smem + STAGES * STAGE_F);
     u64 *empty = full + STAGES;
-    u64 *red_full = empty + STAGES;                 // [2]   gx hand-over between groups
+    u64 *red_full = empty + STAGES;                 // [2]   gx hand-over between logical groups
     u64 *red_free = red_full + 2;                   // [2]
-    float *part = reinterpret_cast<float *>(red_free + 2);       // [STAGES][NCW][16] gY partials of each warp
-    int *arrived = reinterpret_cast<int *>(part + STAGES * NCW * 16);   // [STAGES] warps done with the stage's gY
-    float *red = reinterpret_cast<float *>(arrived + STAGES);    // [2][CG-1][XR][MUL]
+    float *part_buf = reinterpret_cast<float *>(red_free + 2);      // [STAGES][GW][16] gY partials of each warp
+    int *arrived = reinterpret_cast<int *>(part_buf + STAGES * GW * 16);   // [STAGES] warps done with the stage's gY
+    float *red = reinterpret_cast<float *>(arrived + STAGES);       // [2][CG*NP-1][XR][MUL]
     const int tid = threadIdx.x;
     for (int i = tid; i < STAGES; i += blockDim.x) arrived[i] = 0;
-    init_barriers(full, empty, STAGES, NCW, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
+    init_barriers(full, empty, STAGES, GW, red_full, 2, CG * NP > 1 ? (CG * NP - 1) * NCW : 1, red_free, 2, NCW);
 
-    if (tid >= CG * GT) {
+    if (tid >= CG * GTH) {
         u32 it = 0;
         auto issue = [&](u32 st, long long e, long long r, u64 *bar) {
             float *stage = smem + st * STAGE_F;
@@ -385,81 +507,15 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         return;
     }
 
-    const int grp = tid / GT, u0 = tid % GT, warp = u0 >> 5, lane = tid & 31;
-    u32 it = 0, node_it = 0;
-    long long n0, n1;
-    node_range(n_nodes, n0, n1);
-    for (long long s = n0; s < n1; ++s, ++node_it) {
-        float xs[CPT][XR], gxa[CPT][XR];
-#pragma unroll
-        for (int q = 0; q < CPT; ++q) {
-            load_x(x + s * X_DIM, u0 + q * GT, xs[q]);
-#pragma unroll
-            for (int i = 0; i < XR; ++i) gxa[q][i] = 0.0f;
-        }
-        const int p0 = rowptr[s], p1 = rowptr[s + 1];
-        for (int p = p0; p < p1; ++p, ++it) {
-            if (it % CG != (u32)grp) continue;      // ring position it is always group it % CG's (STAGES % CG == 0)
-            const u32 st = it % STAGES, ph = (it / STAGES) & 1;
-            if (!mbar_wait(&full[st], ph)) {
-                if (lane == 0) atomicExch(&mmk_status, 4);
-                return;
-            }
-            const float *stage = smem + st * STAGE_F;
-            long long e = *reinterpret_cast<const long long *>(stage + W_DIM + OUT_DIM + 16);
-            MMK_CHECK_INDEX(e, n_edges, 3);
-            float y[YD], gy[16];
-            load_y(stage + W_DIM + OUT_DIM, Y, e, y);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) gy[j] = 0.0f;
-#pragma unroll
-            for (int q = 0; q < CPT; ++q) {
-                const int u = u0 + q * GT;
-                float w[NINS], go[ORR], gw[NINS];
-#pragma unroll
-                for (int k = 0; k < NINS; ++k) w[k] = stage[k * MUL + u];
-                load_out_s(stage + W_DIM, u, go);
-                bwd_edge(xs[q], y, w, go, gxa[q], gw, gy);
-                if (gW != nullptr) {
-                    float *gwe = gW + e * W_DIM + u;
-#pragma unroll
-                    for (int k = 0; k < NINS; ++k) gwe[k * MUL] = gw[k];
-                }
-            }
-            if (gY != nullptr) {
-                // channel sum of gY[e]: each warp reduces its channels in registers and leaves 16 partials in the
-                // stage's slot; the warp that finishes last adds the NCW partials in warp order (deterministic),
-                // writes gY[e] and clears the counter.  The stage is released only afterwards, so the slot is free.
-                float *pb = part + (size_t)st * NCW * 16;
-                const float v = warp_transpose_reduce16(gy);
-                if ((lane & 1) == 0) pb[warp * 16 + (lane >> 1)] = v;
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) {
-                    __threadfence_block();
-                    last = atomicAdd(&arrived[st], 1) == (int)NCW - 1;
-                    if (last) __threadfence_block();
-                }
-                if (__shfl_sync(0xffffffffu, last, 0)) {
-                    if (lane < YD) {
-                        float t = 0.0f;
-#pragma unroll
-                        for (int w8 = 0; w8 < (int)NCW; ++w8) t += pb[w8 * 16 + lane];
-                        gY[e * YD + lane] = t;
-                    }
-                    if (lane == 0) arrived[st] = 0;
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
-        }
-        if (!reduce_groups<CG, CPT, XR>(red_full, red_free, red, grp, u0, node_it, gxa)) {
-            if (lane == 0) atomicExch(&mmk_status, 9);
-            return;
-        }
-        if (gx != nullptr && grp == 0) {
-#pragma unroll
-            for (int q = 0; q < CPT; ++q) store_x(gx + s * X_DIM, u0 + q * GT, gxa[q]);
-        }
+    const int grp = tid / GTH, part = (tid % GTH) / GT, u0 = tid % GT;
+    const int gwarp = (tid % GTH) >> 5, lane = tid & 31;   // warp index within the group (all parts)
+    const int lg = grp * NP + part;                        // logical group of the gx sum
+    if (part == 0) bwd_consume<STAGES, CG, CPT, NP, 0>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, grp, lg, u0, gwarp, lane);
+    if constexpr (NP > 1) {
+        if (part == 1) bwd_consume<STAGES, CG, CPT, NP, 1>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, grp, lg, u0, gwarp, lane);
+    }
+    if constexpr (NP > 2) {
+        if (part == 2) bwd_consume<STAGES, CG, CPT, NP, 2>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, grp, lg, u0, gwarp, lane);
+        if (part == 3) bwd_consume<STAGES, CG, CPT, NP, 3>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, grp, lg, u0, gwarp, lane);
     }
 }

@@ -54,12 +54,17 @@ PLAN_VARIANTS = [
     {'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2'},
     {'MMK_CONV_FWD_CPT': '4', 'MMK_CONV_BWD_CPT': '4', 'MMK_CONV_FWD_CG': '8', 'MMK_CONV_BWD_CG': '8'},
     {'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2', 'MMK_CONV_FWD_CG': '8', 'MMK_CONV_BWD_CG': '8'},
-    {'MMK_CONV_BWD_FORM': '0', 'MMK_CONV_SMEM_KB': '220', 'MMK_CONV_FWD_CG': '1', 'MMK_CONV_BWD_CG': '1'},
+    {'MMK_CONV_BWD_FORM': '0', 'MMK_CONV_SMEM_KB': '200', 'MMK_CONV_FWD_CG': '1', 'MMK_CONV_BWD_CG': '1'},
+    {'MMK_CONV_FWD_NP': '2', 'MMK_CONV_BWD_NP': '2'},
+    {'MMK_CONV_FWD_NP': '4', 'MMK_CONV_BWD_NP': '4', 'MMK_CONV_BWD_CG': '1', 'MMK_CONV_BWD_MINB': '1'},
+    {'MMK_CONV_FWD_NP': '2', 'MMK_CONV_BWD_NP': '2', 'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2',
+     'MMK_CONV_FWD_MINB': '2'},
 ]
 
 
 @pytest.mark.parametrize('env', PLAN_VARIANTS, ids=lambda e: ','.join(f'{k[9:]}={v}' for k, v in e.items()))
-@pytest.mark.parametrize('hidden,N,E', [('128x0e', 1500, 30000), ('128x0e+128x1o', 300, 6000)])
+@pytest.mark.parametrize('hidden,N,E', [('128x0e', 1500, 30000), ('128x0e+128x1o', 300, 6000),
+                                         ('128x0e+128x1o+128x2e', 120, 2500)])
 def test_conv_plan_variants_match_oracle(cuda, monkeypatch, env, hidden, N, E):
     for k, v in env.items():
         monkeypatch.setenv(k, v)
