@@ -82,6 +82,10 @@ MMK_API int mmk_conv_layer_destroy(mmk_conv_layer *layer);
 MMK_API int mmk_conv_layer_dims(const mmk_conv_layer *layer, int *x_dim, int *y_dim, int *out_dim, int *w_dim);
 /* NVRTC-compile the generated source without loading it (needs no GPU); for build checks and tests. */
 MMK_API int mmk_conv_compile_check(const mmk_conv_desc *desc);
+/* The generated layer header (sizes, launch plan and the straight-line per-edge bodies with the baked coefficients)
+ * for this descriptor, as the reference's ``source(spec)`` returns its generated Metal source (conv.py:105-107).
+ * Copies at most cap bytes (NUL-terminated when it fits) and sets *len to the full length; buf may be NULL. */
+MMK_API int mmk_conv_source(const mmk_conv_desc *desc, char *buf, size_t cap, size_t *len);
 /* Error status of the layer's kernels on the current device (0 = ok; nonzero = a pipeline wait gave up and the kernel
  * returned early, its outputs are invalid).  Synchronises with the device; reset != 0 clears it. */
 MMK_API int mmk_conv_layer_status(const mmk_conv_layer *layer, int32_t *status, int reset);
@@ -138,9 +142,11 @@ MMK_API int mmk_csr_build_noalloc(const int64_t *index, int64_t n_edges, int64_t
 /* Polynomial form of one MACE SymmetricContraction (reference src/mace_mps_kernels/symmetric.py:52-75 ``SCSpec``):
  * for output block q (M_q components, output offset out_off_q = C * sum_{q'<q} M_q'), term t with monomial
  * prod_{i in idx_t} x_i (degree deg_t, indices into the n_ell per-channel components) and first row row_t:
- *   out[b, out_off_q + c*M_q + m] = sum_t T[elem(b), row_t + m, c] * prod_{i in idx_t} x[b, c, i]
- * T is [n_elem, n_rows, CP] fp32 on the device (caller-owned), CP = C rounded up to a multiple of 4 (zero padded), so
- * every row chunk the kernels copy with TMA starts on a 16-byte boundary. */
+ *   out[b, out_off_q + c*M_q + m] = sum_t T[elem(b), c, row_t + m] * prod_{i in idx_t} x[b, c, i]
+ * T is [n_elem, C, RP] fp32 on the device (caller-owned): one column of rows per (element, channel), RP = n_rows
+ * rounded up to a multiple of 4 (zero padded), so every column the kernels copy with TMA starts on a 16-byte
+ * boundary.  (The reference packs T[e][row][c], symmetric.py:71-74; the B200 kernels work node-major and read one
+ * channel's column at a time.) */
 typedef struct mmk_sc_desc {
     int C;                   /* channels                                                             */
     int n_ell;               /* per-channel feature components, (l_max+1)^2                          */
@@ -162,6 +168,9 @@ MMK_API int mmk_sc_layer_create(const mmk_sc_desc *desc, mmk_sc_layer **layer);
 MMK_API int mmk_sc_layer_destroy(mmk_sc_layer *layer);
 MMK_API int mmk_sc_layer_dims(const mmk_sc_layer *layer, int *C, int *n_ell, int *out_dim, int *n_rows);
 MMK_API int mmk_sc_compile_check(const mmk_sc_desc *desc);
+/* The generated layer header (sizes, launch plan, the Horner-scheme term code), as the reference's ``source(spec)``
+ * (symmetric.py:78-80); same buffer contract as mmk_conv_source. */
+MMK_API int mmk_sc_source(const mmk_sc_desc *desc, char *buf, size_t cap, size_t *len);
 
 MMK_API int mmk_sc_layer_status(const mmk_sc_layer *layer, int32_t *status, int reset);
 
@@ -169,7 +178,7 @@ MMK_API int mmk_sc_layer_status(const mmk_sc_layer *layer, int32_t *status, int 
 MMK_API int mmk_elem_index(const float *node_attrs, int64_t n_nodes, int n_elem, int32_t *elem, void *stream);
 /* Nodes grouped by element: perm[erow[e]:erow[e+1]] = the nodes of element e in increasing order (the CSR of elem;
  * workspace: mmk_csr_workspace_bytes(n_elem, n_nodes) bytes).  The symmetric-contraction kernels work on these
- * groups so that one coefficient row feeds several nodes. */
+ * groups so that one coefficient column feeds 32 nodes at a time. */
 MMK_API int mmk_elem_groups(const int32_t *elem, int64_t n_nodes, int n_elem, int32_t *erow, int32_t *perm,
                             void *workspace, size_t workspace_bytes, void *stream);
 

@@ -40,6 +40,7 @@ SIGNATURES = {
     'mmk_conv_layer_destroy': (_i, [_p]),
     'mmk_conv_layer_dims': (_i, [_p, _ip, _ip, _ip, _ip]),
     'mmk_conv_compile_check': (_i, [ctypes.POINTER(ConvDesc)]),
+    'mmk_conv_source': (_i, [ctypes.POINTER(ConvDesc), ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     'mmk_conv_layer_status': (_i, [_p, _ip, _i]),
     'mmk_conv_fwd': (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p]),
     'mmk_conv_bwd': (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p]),
@@ -50,6 +51,7 @@ SIGNATURES = {
     'mmk_sc_layer_destroy': (_i, [_p]),
     'mmk_sc_layer_dims': (_i, [_p, _ip, _ip, _ip, _ip]),
     'mmk_sc_compile_check': (_i, [ctypes.POINTER(SCDesc)]),
+    'mmk_sc_source': (_i, [ctypes.POINTER(SCDesc), ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     'mmk_sc_layer_status': (_i, [_p, _ip, _i]),
     'mmk_elem_index': (_i, [_p, _i64, _i, _p, _p]),
     'mmk_elem_groups': (_i, [_p, _i64, _i, _p, _p, _p, _sz, _p]),
@@ -120,3 +122,12 @@ def int_array(vals):
 def double_array(vals):
     vals = list(vals)
     return (ctypes.c_double * max(1, len(vals)))(*vals)
+
+
+def generated_source(fn_name, desc):
+    """The generated layer header for a descriptor (``mmk_conv_source`` / ``mmk_sc_source``)."""
+    n = ctypes.c_size_t(0)
+    check(getattr(lib(), fn_name)(ctypes.byref(desc), None, 0, ctypes.byref(n)))
+    buf = ctypes.create_string_buffer(n.value + 1)
+    check(getattr(lib(), fn_name)(ctypes.byref(desc), buf, n.value + 1, ctypes.byref(n)))
+    return buf.value.decode()

@@ -164,6 +164,12 @@ _CSR_CACHE = []          # [(weakref(edge_index), version, n_nodes, csr)], most 
 _CSR_CACHE_SIZE = 4
 
 
+def source(spec):
+    """Generated CUDA layer header for ``spec`` (sizes, launch plan and the straight-line per-edge bodies with the
+    probed coefficients), the counterpart of the reference's ``source(spec)`` (conv.py:225)."""
+    return _lib.generated_source('mmk_conv_source', spec.descriptor())
+
+
 def csr_build(index: torch.Tensor, n_nodes: int):
     """(rowptr int32[n+1], eids int32[E]) with eids grouped by ``index`` in increasing edge id, on index's device
     (the reference's ``csr_by``, conv.py:308-314)."""

@@ -1,32 +1,28 @@
 // sc.cuh -- sm_100a kernels of MACE's symmetric contraction evaluated as a precomputed polynomial.
 //
 // Compiled by NVRTC with a generated "mmk_layer.h" that bakes in one SymmetricContraction's monomial list
-// (reference src/mace_mps_kernels/symmetric.py:52-75 builds the same list): sizes CH (channels), CP (channel stride of
-// the coefficient table, CH rounded up to 4), NELL, NROWS, OUTD (output row), OUTM (outputs per channel), the row
-// chunking of the table (NCHUNK chunks of at most RCH rows cut at term boundaries, CHUNK_ROW0[]), and per chunk the
-// straight-line term code sc_fwd_body<GG, TG> / sc_bwd_body<GG, TG> (chunk k run by the group that owns its ring
-// position, taken from and handed back to the ring around its terms), sc_fwd_store<GG>, sc_load_grad<GG>.
+// (reference src/mace_mps_kernels/symmetric.py:52-75 builds the same list): sizes CH (channels), NELL, NROWS, RP (rows
+// rounded up to 4), OUTD (output row), OUTM (outputs per channel), the launch shape SC_NT / SC_CC / STAGES, and the
+// straight-line term code sc_fwd_body / sc_bwd_body (one (node, channel) each, coefficients read as float4 from the
+// channel's column), sc_fwd_store, sc_load_grad.
 //
-// Work: nodes are grouped by element (perm / erow: the node CSR of the element index).  A tile is NG*GG nodes of one
-// element.  The CTA has TG consumer groups of CPG threads (CPG = CH*NG rounded up to whole warps, NG and GG template
-// parameters) and one producer warp.  Thread (group, sub, c) evaluates channel c of the GG nodes of sub-tile `sub` for the chunks whose ring
-// position is group modulo TG; every coefficient T[e, row, c] read from shared memory feeds GG nodes.  The producer streams T[e]
-// chunk by chunk (TMA bulk copies of rows*CP contiguous floats) through a STAGES-deep ring of shared memory, each stage
-// released by the warps of the group that owns it.  With TG > 1 the groups' partial sums are added in shared memory
-// in group order (deterministic), handed over with a pair of mbarriers per tile parity.
-// Two instantiations (GG, NG, TG): many nodes -> one node per thread, NG = 512/CH sub-tiles sharing every staged
-// coefficient row, one group; few nodes -> NG = 128/CH, the term list split over TG = 4 groups.
-// Forward: out[b, off + c*M + m] = sum_t T[e, row_t + m, c] x^idx_t.  Backward: gx[b, c, i] = sum_t (sum_m
-// T[e, row_t + m, c] g[b, off + c*M + m]) d(x^idx_t)/dx_i.  Waits are bounded as in conv_tp.cuh.
+// Coefficient table T[e][c][RP]: one contiguous column of rows per (element, channel).  Row of term t, output m:
+// row_t + m.
+//
+// Work is node-major.  Nodes are grouped by element (perm / erow: the node CSR of the element index).  A unit is
+// (node group of SC_NT*32 nodes of one element, chunk of SC_CC channels).  The CTA has SC_NT*SC_CC consumer warps and
+// one producer warp: warp (t, j) evaluates channel c = chunk*SC_CC + j of the 32 nodes t*32 .. t*32+31 of the group,
+// lane = node.  The producer copies the chunk's SC_CC coefficient columns of element e (SC_CC*RP contiguous floats,
+// one TMA bulk copy) into a STAGES-deep ring; within a warp every coefficient load is a broadcast (all lanes read the
+// same address), so shared-memory bandwidth is not the limit and each 16-byte load feeds four rows of FMAs.
+// Forward: out[b, off + c*M + m] = sum_t T[e, c, row_t + m] x^idx_t.  Backward: gx[b, c, i] = sum_t (sum_m
+// T[e, c, row_t + m] g[b, off + c*M + m]) d(x^idx_t)/dx_i.  Waits are bounded as in conv_tp.cuh.
 #include "mmk_layer.h"
 
 #define MMK_WAIT_BUDGET (2000000000LL)
-
-// consumer threads per group: CH channels x NG node sub-tiles, rounded up to whole warps
-template <int NG>
-struct Cpg {
-    static constexpr int value = ((CH * NG) + 31) / 32 * 32;
-};
+#define SC_NWARP (SC_NT * SC_CC)                      // consumer warps
+#define SC_NCH ((CH + SC_CC - 1) / SC_CC)             // channel chunks
+#define SC_UNIT_NODES (SC_NT * 32)
 
 __device__ int mmk_status;
 
@@ -75,243 +71,178 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, u32 bytes, 
                  : "memory");
 }
 
-// tile t -> (element, first position in perm, node count) for tiles of TN nodes; tiles of one element are consecutive
+// node group g -> (element, first position in perm, node count) for groups of TN nodes; groups of one element are
+// consecutive
 template <int TN>
-__device__ __forceinline__ bool tile_of(long long t, const int *__restrict__ erow, int n_elem, int &e, int &p0, int &cnt) {
+__device__ __forceinline__ bool group_of(long long g, const int *__restrict__ erow, int n_elem, int &e, int &p0,
+                                         int &cnt) {
     long long before = 0;
     for (int k = 0; k < n_elem; ++k) {
         const int a = erow[k], b = erow[k + 1];
-        const long long nt = (b - a + TN - 1) / TN;
-        if (t < before + nt) {
+        const long long ng = (b - a + TN - 1) / TN;
+        if (g < before + ng) {
             e = k;
-            p0 = a + (int)(t - before) * TN;
+            p0 = a + (int)(g - before) * TN;
             cnt = min(TN, b - p0);
             return true;
         }
-        before += nt;
+        before += ng;
     }
     return false;
 }
 
-// shared-memory layout: [STAGES][RCH*CP] coefficient ring | full[STAGES] | empty[STAGES] | red_full[2] | red_free[2]
-//                       | reduction buffer [2][TG-1][GG*K][CPG]
+// shared memory: ring [STAGES][SC_CC][RP] floats | full[STAGES] | empty[STAGES]
 struct Smem {
     float *ring;
-    u64 *full, *empty, *red_full, *red_free;
-    float *red;
+    u64 *full, *empty;
 };
 
-__device__ __forceinline__ Smem smem_layout(float *base) {
+__device__ __forceinline__ Smem smem_setup(float *base) {
     Smem s;
     s.ring = base;
-    s.full = reinterpret_cast<u64 *>(base + STAGES * RCH * CP);
+    s.full = reinterpret_cast<u64 *>(base + (size_t)STAGES * SC_CC * RP);
     s.empty = s.full + STAGES;
-    s.red_full = s.empty + STAGES;
-    s.red_free = s.red_full + 2;
-    s.red = reinterpret_cast<float *>(s.red_free + 2);
-    return s;
-}
-
-template <int NG, int TG>
-__device__ __forceinline__ void sc_setup(const Smem &s) {
-    constexpr int CPG = Cpg<NG>::value;
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&s.full[i], 1);
-            mbar_init(&s.empty[i], CPG / 32);
-        }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&s.red_full[i], TG > 1 ? (TG - 1) * (CPG / 32) : 1);
-            mbar_init(&s.red_free[i], CPG / 32);
+            mbar_init(&s.empty[i], SC_NWARP);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
+    return s;
 }
 
-// Consumer view of the ring for one tile: chunk k of the tile lives in stage (it + k) % STAGES.
-struct Ring {
-    const Smem &s;
-    u32 it;
-    int c;
-    __device__ __forceinline__ const float *wait(int k) {
-        const u32 i = it + k, st = i % STAGES;
-        if (!mbar_wait(&s.full[st], (i / STAGES) & 1)) {
-            if ((threadIdx.x & 31) == 0) atomicExch(&mmk_status, 6);
-            return nullptr;
-        }
-        return s.ring + (size_t)st * RCH * CP + c;
-    }
-    __device__ __forceinline__ void release(int k) {
-        __syncwarp();
-        if ((threadIdx.x & 31) == 0) mbar_arrive(&s.empty[(it + k) % STAGES]);
-    }
-    __device__ __forceinline__ void advance(int n) { it += n; }
-    // group that consumes chunk k of this tile: by ring position, so that (STAGES a multiple of TG) every slot always
-    // belongs to one group and a group never waits on a phase of a slot another group still holds
-    __device__ __forceinline__ int owner(int k, int tg) const { return (int)((it + k) % (u32)tg); }
-};
-
-template <int TN>
+// Producer (lane 0 of the last warp): unit u = (node group u / SC_NCH, channel chunk u % SC_NCH); copy the chunk's
+// coefficient columns of the group's element into ring position it.
 __device__ __forceinline__ void sc_produce(const float *__restrict__ T, const int *__restrict__ erow, int n_elem,
-                                           long long n_tiles, const Smem &s) {
-    const int lane = threadIdx.x & 31;
+                                           long long n_units, const Smem &s) {
+    if ((threadIdx.x & 31) != 0) return;
     u32 it = 0;
     bool ok = true;
-    for (long long t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+    for (long long u = blockIdx.x; u < n_units; u += gridDim.x, ++it) {
         int e, p0, cnt;
-        if (!tile_of<TN>(t, erow, n_elem, e, p0, cnt)) break;
-        const float *Te = T + (size_t)e * NROWS * CP;
-        for (int k = 0; k < NCHUNK && ok; ++k, ++it) {
-            const u32 st = it % STAGES, ph = (it / STAGES) & 1;
-            if (lane == 0) {
-                if (!mbar_wait(&s.empty[st], ph ^ 1)) {
-                    ok = false;
-                    atomicExch(&mmk_status, 7);
-                } else {
-                    const u32 bytes = (u32)(CHUNK_ROW0[k + 1] - CHUNK_ROW0[k]) * CP * 4;
-                    mbar_arrive_expect_tx(&s.full[st], bytes);
-                    bulk_g2s(s.ring + (size_t)st * RCH * CP, Te + (size_t)CHUNK_ROW0[k] * CP, bytes, &s.full[st]);
-                }
-            }
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!group_of<SC_UNIT_NODES>(u / SC_NCH, erow, n_elem, e, p0, cnt)) break;
+        const int c0 = (int)(u % SC_NCH) * SC_CC;
+        const int cols = min(SC_CC, CH - c0);
+        const u32 st = it % STAGES, ph = (it / STAGES) & 1;
+        if (!mbar_wait(&s.empty[st], ph ^ 1)) {
+            ok = false;
+            atomicExch(&mmk_status, 7);
+            break;
         }
+        const u32 bytes = (u32)cols * RP * 4;
+        mbar_arrive_expect_tx(&s.full[st], bytes);
+        bulk_g2s(s.ring + (size_t)st * SC_CC * RP, T + ((size_t)e * CH + c0) * RP, bytes, &s.full[st]);
     }
-    if (!ok && lane == 0) {                       // let the copies already issued land before the CTA exits
+    if (!ok) {                                    // let the copies already issued land before the CTA exits
         const u32 first = it > STAGES ? it - STAGES : 0;
         for (u32 i = first; i < it; ++i) mbar_wait(&s.full[i % STAGES], (i / STAGES) & 1);
     }
 }
 
-// Add the groups' partial sums v[GG][K] of one tile into group 0 (fixed group order).  The buffer half used by
-// tile_it is refilled two tiles later only after group 0 has released it (red_free).  False on a timeout.
-template <int GG, int NG, int TG, int K>
-__device__ __forceinline__ bool reduce_groups(const Smem &s, int grp, int r, u32 tile_it, float (&v)[GG][K]) {
-    constexpr int CPG = Cpg<NG>::value;
-    if constexpr (TG == 1) {
-        return true;
-    } else {
-        const u32 par = tile_it & 1, ph = (tile_it >> 1) & 1;
-        float *buf = s.red + (size_t)par * (TG - 1) * GG * K * CPG;
-        const int lane = threadIdx.x & 31;
-        if (grp > 0) {
-            if (!mbar_wait(&s.red_free[par], ph ^ 1)) return false;
-            float *dst = buf + (size_t)(grp - 1) * GG * K * CPG + r;
-#pragma unroll
-            for (int j = 0; j < GG; ++j)
-#pragma unroll
-                for (int i = 0; i < K; ++i) dst[(j * K + i) * CPG] = v[j][i];
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.red_full[par]);
-        } else {
-            if (!mbar_wait(&s.red_full[par], ph)) return false;
-#pragma unroll
-            for (int q = 0; q < TG - 1; ++q) {
-                const float *src = buf + (size_t)q * GG * K * CPG + r;
-#pragma unroll
-                for (int j = 0; j < GG; ++j)
-#pragma unroll
-                    for (int i = 0; i < K; ++i) v[j][i] += src[(j * K + i) * CPG];
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.red_free[par]);
-        }
-        return true;
+// Consumer view of one unit: the node of this lane (-1 if none) and the channel of this warp (>= CH if none).
+struct Unit {
+    long long node;
+    int c;
+    bool ok;
+};
+
+__device__ __forceinline__ Unit unit_of(long long u, const int *__restrict__ perm, const int *__restrict__ erow,
+                                        int n_elem, long long n_nodes) {
+    Unit r{-1, CH, false};
+    int e, p0, cnt;
+    if (!group_of<SC_UNIT_NODES>(u / SC_NCH, erow, n_elem, e, p0, cnt)) return r;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = warp / SC_CC, j = warp % SC_CC;
+    const int q = t * 32 + lane;
+    r.ok = true;
+    r.c = (int)(u % SC_NCH) * SC_CC + j;
+    if (q < cnt) {
+        r.node = perm[p0 + q];
+        if (MMK_BAD_INDEX(r.node, n_nodes, 11)) r.node = -1;
     }
+    return r;
 }
 
-template <int GG, int NG, int TG>
-__global__ void __launch_bounds__(TG * Cpg<NG>::value + 32)
+template <int NT, int CC>
+__global__ void __launch_bounds__(NT * CC * 32 + 32, SC_MINB)
 mmk_sc_fwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, const int *__restrict__ erow, int n_elem,
-                  const float *__restrict__ T, float *__restrict__ out, long long n_tiles, long long n_nodes) {
+                  const float *__restrict__ T, float *__restrict__ out, long long n_units, long long n_nodes) {
+    static_assert(NT == SC_NT && CC == SC_CC, "launch shape of the generated header");
     extern __shared__ __align__(128) float smem[];
-    constexpr int CPG = Cpg<NG>::value;
-    const Smem s = smem_layout(smem);
-    sc_setup<NG, TG>(s);
-    const int tid = threadIdx.x;
-    if (tid >= TG * CPG) {
-        sc_produce<NG * GG>(T, erow, n_elem, n_tiles, s);
+    const Smem s = smem_setup(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp == SC_NWARP) {
+        sc_produce(T, erow, n_elem, n_units, s);
         return;
     }
-    const int grp = tid / CPG, r = tid % CPG, c = r % CH, sub = r / CH;
-    const int lane = tid & 31;
-    Ring ring{s, 0u, c};
-    u32 tile_it = 0;
-    for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tile_it) {
-        int e, p0, cnt;
-        if (!tile_of<NG * GG>(t, erow, n_elem, e, p0, cnt)) break;
-        long long nodes[GG];
-        float xv[GG][NELL], acc[GG][OUTM];
+    const int j = warp % SC_CC;
+    u32 it = 0;
+    for (long long u = blockIdx.x; u < n_units; u += gridDim.x, ++it) {
+        const Unit un = unit_of(u, perm, erow, n_elem, n_nodes);
+        if (!un.ok) break;
+        const bool active = un.node >= 0 && un.c < CH;
+        float xv[NELL], acc[OUTM];
+        if (active) {
+            load_feat(x + (un.node * CH + un.c) * NELL, xv);
+        } else {
 #pragma unroll
-        for (int j = 0; j < GG; ++j) {
-            const int q = sub * GG + j;
-            nodes[j] = (sub < NG && q < cnt) ? (long long)perm[p0 + q] : -1;
-            if (nodes[j] >= 0 && MMK_BAD_INDEX(nodes[j], n_nodes, 11)) nodes[j] = -1;
-            if (nodes[j] >= 0) {
-                load_feat(x + (nodes[j] * CH + c) * NELL, xv[j]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < NELL; ++i) xv[j][i] = 0.0f;
-            }
-#pragma unroll
-            for (int i = 0; i < OUTM; ++i) acc[j][i] = 0.0f;
+            for (int i = 0; i < NELL; ++i) xv[i] = 0.0f;
         }
-        if (!sc_fwd_body<GG, TG>(ring, grp, xv, acc)) return;
-        if (!reduce_groups<GG, NG, TG, OUTM>(s, grp, r, tile_it, acc)) {
-            if (lane == 0) atomicExch(&mmk_status, 8);
+#pragma unroll
+        for (int i = 0; i < OUTM; ++i) acc[i] = 0.0f;
+        const u32 st = it % STAGES;
+        if (!mbar_wait(&s.full[st], (it / STAGES) & 1)) {
+            if (lane == 0) atomicExch(&mmk_status, 6);
             return;
         }
-        if (grp == 0) sc_fwd_store<GG>(acc, nodes, out, c);
+        if (un.c < CH) sc_fwd_body(s.ring + ((size_t)st * SC_CC + j) * RP, xv, acc);   // warp-uniform
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.empty[st]);
+        if (active) sc_fwd_store(acc, un.node, out, un.c);
     }
 }
 
-template <int GG, int NG, int TG>
-__global__ void __launch_bounds__(TG * Cpg<NG>::value + 32)
+template <int NT, int CC>
+__global__ void __launch_bounds__(NT * CC * 32 + 32, SC_MINB)
 mmk_sc_bwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, const int *__restrict__ erow, int n_elem,
-                  const float *__restrict__ T, const float *__restrict__ g, float *__restrict__ gx, long long n_tiles,
+                  const float *__restrict__ T, const float *__restrict__ g, float *__restrict__ gx, long long n_units,
                   long long n_nodes) {
+    static_assert(NT == SC_NT && CC == SC_CC, "launch shape of the generated header");
     extern __shared__ __align__(128) float smem[];
-    constexpr int CPG = Cpg<NG>::value;
-    const Smem s = smem_layout(smem);
-    sc_setup<NG, TG>(s);
-    const int tid = threadIdx.x;
-    if (tid >= TG * CPG) {
-        sc_produce<NG * GG>(T, erow, n_elem, n_tiles, s);
+    const Smem s = smem_setup(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp == SC_NWARP) {
+        sc_produce(T, erow, n_elem, n_units, s);
         return;
     }
-    const int grp = tid / CPG, r = tid % CPG, c = r % CH, sub = r / CH;
-    const int lane = tid & 31;
-    Ring ring{s, 0u, c};
-    u32 tile_it = 0;
-    for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tile_it) {
-        int e, p0, cnt;
-        if (!tile_of<NG * GG>(t, erow, n_elem, e, p0, cnt)) break;
-        long long nodes[GG];
-        float xv[GG][NELL], gv[GG][OUTM], d[GG][NELL];
+    const int j = warp % SC_CC;
+    u32 it = 0;
+    for (long long u = blockIdx.x; u < n_units; u += gridDim.x, ++it) {
+        const Unit un = unit_of(u, perm, erow, n_elem, n_nodes);
+        if (!un.ok) break;
+        const bool active = un.node >= 0 && un.c < CH;
+        float xv[NELL], gv[OUTM], d[NELL];
+        if (active) {
+            load_feat(x + (un.node * CH + un.c) * NELL, xv);
+            sc_load_grad(g, un.node, un.c, gv);
+        } else {
 #pragma unroll
-        for (int j = 0; j < GG; ++j) {
-            const int q = sub * GG + j;
-            nodes[j] = (sub < NG && q < cnt) ? (long long)perm[p0 + q] : -1;
-            if (nodes[j] >= 0 && MMK_BAD_INDEX(nodes[j], n_nodes, 11)) nodes[j] = -1;
-            if (nodes[j] >= 0) {
-                load_feat(x + (nodes[j] * CH + c) * NELL, xv[j]);
-            } else {
+            for (int i = 0; i < NELL; ++i) xv[i] = 0.0f;
 #pragma unroll
-                for (int i = 0; i < NELL; ++i) xv[j][i] = 0.0f;
-            }
-#pragma unroll
-            for (int i = 0; i < NELL; ++i) d[j][i] = 0.0f;
+            for (int i = 0; i < OUTM; ++i) gv[i] = 0.0f;
         }
-        sc_load_grad<GG>(g, nodes, c, gv);
-        if (!sc_bwd_body<GG, TG>(ring, grp, xv, gv, d)) return;
-        if (!reduce_groups<GG, NG, TG, NELL>(s, grp, r, tile_it, d)) {
-            if (lane == 0) atomicExch(&mmk_status, 8);
+#pragma unroll
+        for (int i = 0; i < NELL; ++i) d[i] = 0.0f;
+        const u32 st = it % STAGES;
+        if (!mbar_wait(&s.full[st], (it / STAGES) & 1)) {
+            if (lane == 0) atomicExch(&mmk_status, 6);
             return;
         }
-        if (grp == 0) {
-#pragma unroll
-            for (int j = 0; j < GG; ++j)
-                if (nodes[j] >= 0) store_feat(gx + (nodes[j] * CH + c) * NELL, d[j]);
-        }
+        if (un.c < CH) sc_bwd_body(s.ring + ((size_t)st * SC_CC + j) * RP, xv, gv, d);   // warp-uniform
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.empty[st]);
+        if (active) store_feat(gx + (un.node * CH + un.c) * NELL, d);
     }
 }

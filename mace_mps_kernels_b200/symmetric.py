@@ -5,13 +5,14 @@ component M the contraction is a polynomial in the channel's features x = x[b, c
     out[b, c, M] = sum_{nu} sum_{i1 <= .. <= i_nu} T_nu[e, c, M, i] x_i1 .. x_i_nu
 with T_nu = U_nu . W_nu symmetrised over index order (the reference's construction, symmetric.py:20-39; here the
 symmetrisation is one matrix product with the 0/1 map "index tuple -> sorted tuple").  Terms whose coefficient
-vanishes for every (e, M, c) are dropped (tolerance 1e-12, symmetric.py:66).  Coefficients are packed as
-T[e][row][c] (row = term's first row + M) so the channel threads of a node read consecutive addresses; terms are
-ordered by degree (descending) then index tuple, as in the reference (symmetric.py:64-69).
+vanishes for every (e, M, c) are dropped (tolerance 1e-12, symmetric.py:66).  ``SCSpec.T`` is packed as the reference
+does, T[e][row][c] (row = term's first row + M); terms are ordered by degree (descending) then index tuple, as in the
+reference (symmetric.py:64-69).  The device copy the kernels read is channel-major, T[e][c][row] with the rows padded
+to a multiple of 4 (``device_table``).
 
 The CUDA kernels (monomial list baked into NVRTC-compiled code) evaluate the polynomial (forward) and its derivative
-(first-order backward) on tiles of nodes of one element, each coefficient row staged once in shared memory by TMA and
-applied to several nodes; double backward raises.
+(first-order backward) node-major: a warp is 32 nodes of one element and one channel, the channel's coefficient column
+is staged in shared memory by TMA and every coefficient load is a broadcast; double backward raises.
 """
 from __future__ import annotations
 
@@ -145,6 +146,12 @@ class SCSpec:
 _ELEM_CACHE = []
 
 
+def source(spec):
+    """Generated CUDA layer header for ``spec`` (sizes, launch plan and the Horner-scheme term code), the counterpart
+    of the reference's ``source(spec)`` (symmetric.py:82)."""
+    return _lib.generated_source('mmk_sc_source', spec.descriptor())
+
+
 def element_groups(node_attrs: torch.Tensor):
     """(elem int32[N], erow int32[n_elem+1], perm int32[N]): the argmax element of every node (reference
     symmetric.py:169) and the nodes grouped by element, on the device; cached per node_attrs tensor and version."""
@@ -202,18 +209,22 @@ class _SCFn(torch.autograd.Function):
         return gx, None, None, None
 
 
+def device_table(T):
+    """[n_elem, rows, C] (SCSpec.T) -> the kernels' layout [n_elem, C, RP], RP = rows rounded up to 4 (zero rows)."""
+    T = torch.as_tensor(T, dtype=torch.float32).transpose(1, 2)
+    rp = (T.shape[2] + 3) // 4 * 4
+    if rp != T.shape[2]:
+        T = torch.nn.functional.pad(T, (0, rp - T.shape[2]))
+    return T.contiguous()
+
+
 class CudaSymmetricContraction(torch.nn.Module):
     """Drop-in for mace ``SymmetricContraction`` at inference: forward(x[N, C, n_ell], node_attrs[N, n_elem])."""
 
     def __init__(self, sc, device='cuda', spec=None):
         super().__init__()
         self.spec = SCSpec(sc) if spec is None else spec
-        # the kernels read T with a channel stride rounded up to 4 floats (16-byte rows for the TMA copies)
-        T = self.spec.T
-        cp = (T.shape[2] + 3) // 4 * 4
-        if cp != T.shape[2]:
-            T = torch.nn.functional.pad(T, (0, cp - T.shape[2]))
-        self.register_buffer('T', T.to(device).contiguous())
+        self.register_buffer('T', device_table(self.spec.T).to(device))
         self._h = _LayerHandle('mmk_sc_layer_create', 'mmk_sc_layer_destroy', self.spec.descriptor())
         self.irreps_in = getattr(sc, 'irreps_in', None)
         self.irreps_out = getattr(sc, 'irreps_out', None)
