@@ -31,7 +31,6 @@ import copy
 import json
 import math
 import os
-import subprocess
 import sys
 import threading
 import time
@@ -77,51 +76,62 @@ def config_dict(n_atoms, n_edges, world):
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """SM clock, power and clock-event reasons of this rank's GPU, sampled every 20 ms by a thread through NVML (read
+    only) during a timed region (no samples, and None in the summary, where NVML is unavailable)."""
 
-    FIELDS = 'clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,' \
-             'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,' \
-             'clocks_event_reasons.sw_power_cap'
+    REASONS = [('hw_slowdown', 'nvmlClocksEventReasonHwSlowdown'),
+               ('hw_thermal_slowdown', 'nvmlClocksEventReasonHwThermalSlowdown'),
+               ('sw_thermal_slowdown', 'nvmlClocksEventReasonSwThermalSlowdown'),
+               ('sw_power_cap', 'nvmlClocksEventReasonSwPowerCap')]
 
     def __init__(self, index):
         self.index = index
-        self.proc = None
+        self.sm, self.mx, self.power, self.reasons = [], None, [], set()
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _handle(self, nv):
+        try:
+            pr = torch.cuda.get_device_properties(self.index)
+            return nv.nvmlDeviceGetHandleByPciBusId(f'{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0')
+        except Exception:                                        # noqa: BLE001
+            return nv.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _loop(self, nv, h):
+        bits = [(name, getattr(nv, const)) for name, const in self.REASONS]
+        while not self._stop.is_set():
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                self.power.append(nv.nvmlDeviceGetPowerUsage(h) / 1000.0)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for name, bit in bits:
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:                                    # noqa: BLE001
+                pass
+            self._stop.wait(0.02)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
-                                          '-lms', '50', '-i', str(self.index)], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self._thread = threading.Thread(target=self._loop, args=(nv, h), daemon=True)
+            self._thread.start()
+        except Exception:                                        # noqa: BLE001
+            self._thread = None
         return self
 
     def __exit__(self, *a):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
-        for l in getattr(self, 'lines', []):
-            f = [x.strip() for x in l.split(',')]
-            try:
-                sm.append(float(f[0]))
-                mx = float(f[1])
-            except (ValueError, IndexError):
-                continue
-            for n, v in zip(names, f[3:7]):
-                if v.lower() == 'active':
-                    reasons.add(n)
-        return {'sm_mhz': float(np.median(sm)) if sm else None, 'sm_max_mhz': mx, 'reasons': sorted(reasons),
-                'samples': len(sm)}
+        return {'sm_mhz': float(np.median(self.sm)) if self.sm else None, 'sm_max_mhz': self.mx,
+                'reasons': sorted(self.reasons), 'samples': len(self.sm),
+                'power_w_max': round(max(self.power), 1) if self.power else None}
 
 
 def flush_l2(buf):
@@ -476,7 +486,9 @@ def main():
     large, roof_large, fp32 = None, None, None
     if not a.no_large and rank == 0:
         cases, info = large_cases(dev, a.large_cells)
-        large = dict(info, ops=time_cases(cases, max(3, a.op_reps // 4), flush))
+        with ClockSampler(local) as clk_large:
+            large_ops = time_cases(cases, max(3, a.op_reps // 4), flush)
+        large = dict(info, ops=large_ops, clocks=clk_large.summary())
         del cases
         big = max((o for o in large['ops'] if o['kind'] == 'conv'), key=lambda o: o['fwd_us'] + o['bwd_us'])
         roof_large = conv_roof(big, 'inputs far larger than L2 (bulk Cu, configs[4] architecture)')

@@ -134,12 +134,17 @@ __device__ __forceinline__ float warp_transpose_reduce16(float (&v)[16]) {
     return v[0];
 }
 
-// Work split: CTA b owns the contiguous node range [b*N/G, (b+1)*N/G) (G = gridDim.x).  With atoms ordered along a
-// space-filling curve a range is a compact domain, so consecutive nodes of a CTA gather mostly the same neighbour rows
-// (L2 hits), and the CTA's edges are one contiguous stretch of the CSR.
-__device__ __forceinline__ void node_range(long long n_nodes, long long &n0, long long &n1) {
-    n0 = (long long)blockIdx.x * n_nodes / gridDim.x;
-    n1 = ((long long)blockIdx.x + 1) * n_nodes / gridDim.x;
+// Work split: the nodes are cut into chunks of nb consecutive nodes and CTA b takes chunks b, b + G, b + 2G, ...
+// (G = gridDim.x).  The host picks nb: either N / G (one contiguous range per CTA: a compact domain when atoms are
+// ordered along a space-filling curve, its edges one stretch of the CSR) or a few nodes (all CTAs then work inside one
+// compact window of G*nb atoms at a time, so the rows they gather stay in L2).  Every chunk is a contiguous stretch of
+// the CSR.
+__device__ __forceinline__ bool next_chunk(long long &c, long long nb, long long n_nodes, long long &n0, long long &n1) {
+    if (c * nb >= n_nodes) return false;
+    n0 = c * nb;
+    n1 = min(n_nodes, n0 + nb);
+    c += gridDim.x;
+    return true;
 }
 
 // Producer: stream the TMA copies of the CTA's edges [rowptr[n0], rowptr[n1]) in CSR order.  The warp fetches the
@@ -279,12 +284,13 @@ __device__ __forceinline__ void init_barriers(u64 *full, u64 *empty, int stages,
 template <int STAGES, int CG, int CPT, int NP, int H>
 __device__ __forceinline__ void fwd_consume(const float *smem, u64 *full, u64 *empty, u64 *red_full, u64 *red_free,
                                             float *red, const float *__restrict__ Y, const int *__restrict__ rowptr,
-                                            float *__restrict__ out, long long n_nodes, int grp, int u0, int lane) {
+                                            float *__restrict__ out, long long n_nodes, long long nb, int grp,
+                                            int u0, int lane) {
     constexpr int GT = MUL / CPT;
     constexpr u32 STAGE_F = W_DIM + X_DIM + 20;
     u32 it = 0, node_it = 0;
-    long long n0, n1;
-    node_range(n_nodes, n0, n1);
+    long long chunk = blockIdx.x, n0, n1;
+    while (next_chunk(chunk, nb, n_nodes, n0, n1))
     for (long long n = n0; n < n1; ++n, ++node_it) {
         float acc[CPT][ORR];
 #pragma unroll
@@ -332,7 +338,7 @@ __global__ void MMK_FWD_BOUNDS(CG * NP * (MUL / CPT) + 32)
 mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ senders, float *__restrict__ out, long long n_nodes,
-                    long long n_edges) {
+                    long long n_edges, long long nb) {
     static_assert(NP == 1 || CG == 1, "a forward split over parts runs one consumer group");
     constexpr int GT = MUL / CPT;                   // threads of one part of a group
     constexpr u32 NCW = GT / 32;                    // warps of one part
@@ -357,22 +363,24 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
             bulk_g2s(stage + W_DIM, x + s * X_DIM, X_DIM * 4, bar);
             if constexpr (Y_TMA) bulk_g2s(stage + W_DIM + X_DIM, Y + e * YD, YD * 4, bar);
         };
-        long long n0, n1;
-        node_range(n_nodes, n0, n1);
-        if (!produce<STAGES>(rowptr, eids, senders, n0, n1, n_nodes, n_edges, full, empty, it, issue) &&
-            (tid & 31) == 0)
-            atomicExch(&mmk_status, 1);
+        long long chunk = blockIdx.x, n0, n1;
+        while (next_chunk(chunk, nb, n_nodes, n0, n1)) {
+            if (!produce<STAGES>(rowptr, eids, senders, n0, n1, n_nodes, n_edges, full, empty, it, issue)) {
+                if ((tid & 31) == 0) atomicExch(&mmk_status, 1);
+                break;
+            }
+        }
         return;
     }
 
     const int grp = tid / GTH, part = (tid % GTH) / GT, u0 = tid % GT, lane = tid & 31;
-    if (part == 0) fwd_consume<STAGES, CG, CPT, NP, 0>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, grp, u0, lane);
+    if (part == 0) fwd_consume<STAGES, CG, CPT, NP, 0>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, nb, grp, u0, lane);
     if constexpr (NP > 1) {
-        if (part == 1) fwd_consume<STAGES, CG, CPT, NP, 1>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, grp, u0, lane);
+        if (part == 1) fwd_consume<STAGES, CG, CPT, NP, 1>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, nb, grp, u0, lane);
     }
     if constexpr (NP > 2) {
-        if (part == 2) fwd_consume<STAGES, CG, CPT, NP, 2>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, grp, u0, lane);
-        if (part == 3) fwd_consume<STAGES, CG, CPT, NP, 3>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, grp, u0, lane);
+        if (part == 2) fwd_consume<STAGES, CG, CPT, NP, 2>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, nb, grp, u0, lane);
+        if (part == 3) fwd_consume<STAGES, CG, CPT, NP, 3>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, nb, grp, u0, lane);
     }
 }
 
@@ -385,14 +393,14 @@ __device__ __forceinline__ void bwd_consume(const float *smem, u64 *full, u64 *e
                                             float *red, float *part_buf, int *arrived, const float *__restrict__ x,
                                             const float *__restrict__ Y, const int *__restrict__ rowptr,
                                             float *__restrict__ gx, float *__restrict__ gY, float *__restrict__ gW,
-                                            long long n_nodes, long long n_edges, int grp, int lg, int u0, int gwarp,
-                                            int lane) {
+                                            long long n_nodes, long long n_edges, long long nb, int grp, int lg,
+                                            int u0, int gwarp, int lane) {
     constexpr int GT = MUL / CPT;
     constexpr u32 GW = NP * (GT / 32);
     constexpr u32 STAGE_F = W_DIM + OUT_DIM + 20;
     u32 it = 0, node_it = 0;
-    long long n0, n1;
-    node_range(n_nodes, n0, n1);
+    long long chunk = blockIdx.x, n0, n1;
+    while (next_chunk(chunk, nb, n_nodes, n0, n1))
     for (long long s = n0; s < n1; ++s, ++node_it) {
         float xs[CPT][XR], gxa[CPT][XR];
 #pragma unroll
@@ -471,7 +479,7 @@ __global__ void MMK_BWD_BOUNDS(CG * NP * (MUL / CPT) + 32)
 mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const float *__restrict__ g, const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ receivers, float *__restrict__ gx, float *__restrict__ gY,
-                    float *__restrict__ gW, long long n_nodes, long long n_edges) {
+                    float *__restrict__ gW, long long n_nodes, long long n_edges, long long nb) {
     constexpr int GT = MUL / CPT;                   // threads of one part of a group
     constexpr u32 NCW = GT / 32;                    // warps of one part
     constexpr int GTH = NP * GT;                    // threads of one group
@@ -499,23 +507,25 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
             bulk_g2s(stage + W_DIM, g + r * OUT_DIM, OUT_DIM * 4, bar);
             if constexpr (Y_TMA) bulk_g2s(stage + W_DIM + OUT_DIM, Y + e * YD, YD * 4, bar);
         };
-        long long n0, n1;
-        node_range(n_nodes, n0, n1);
-        if (!produce<STAGES>(rowptr, eids, receivers, n0, n1, n_nodes, n_edges, full, empty, it, issue) &&
-            (tid & 31) == 0)
-            atomicExch(&mmk_status, 3);
+        long long chunk = blockIdx.x, n0, n1;
+        while (next_chunk(chunk, nb, n_nodes, n0, n1)) {
+            if (!produce<STAGES>(rowptr, eids, receivers, n0, n1, n_nodes, n_edges, full, empty, it, issue)) {
+                if ((tid & 31) == 0) atomicExch(&mmk_status, 3);
+                break;
+            }
+        }
         return;
     }
 
     const int grp = tid / GTH, part = (tid % GTH) / GT, u0 = tid % GT;
     const int gwarp = (tid % GTH) >> 5, lane = tid & 31;   // warp index within the group (all parts)
     const int lg = grp * NP + part;                        // logical group of the gx sum
-    if (part == 0) bwd_consume<STAGES, CG, CPT, NP, 0>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, grp, lg, u0, gwarp, lane);
+    if (part == 0) bwd_consume<STAGES, CG, CPT, NP, 0>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, grp, lg, u0, gwarp, lane);
     if constexpr (NP > 1) {
-        if (part == 1) bwd_consume<STAGES, CG, CPT, NP, 1>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, grp, lg, u0, gwarp, lane);
+        if (part == 1) bwd_consume<STAGES, CG, CPT, NP, 1>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, grp, lg, u0, gwarp, lane);
     }
     if constexpr (NP > 2) {
-        if (part == 2) bwd_consume<STAGES, CG, CPT, NP, 2>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, grp, lg, u0, gwarp, lane);
-        if (part == 3) bwd_consume<STAGES, CG, CPT, NP, 3>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, grp, lg, u0, gwarp, lane);
+        if (part == 2) bwd_consume<STAGES, CG, CPT, NP, 2>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, grp, lg, u0, gwarp, lane);
+        if (part == 3) bwd_consume<STAGES, CG, CPT, NP, 3>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, grp, lg, u0, gwarp, lane);
     }
 }

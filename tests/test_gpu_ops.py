@@ -59,6 +59,7 @@ PLAN_VARIANTS = [
     {'MMK_CONV_FWD_NP': '4', 'MMK_CONV_BWD_NP': '4', 'MMK_CONV_BWD_CG': '1', 'MMK_CONV_BWD_MINB': '1'},
     {'MMK_CONV_FWD_NP': '2', 'MMK_CONV_BWD_NP': '2', 'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2',
      'MMK_CONV_FWD_MINB': '2'},
+    {'MMK_CONV_FWD_NB': '3', 'MMK_CONV_BWD_NB': '5'},
 ]
 
 
