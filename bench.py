@@ -260,6 +260,18 @@ def step_cases(model, batch):
 
 LARGE_CELLS = 16
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum, forward + backward launch) of the conv layers from the
+# ncu launch lists summarised in profiles/ef_step_cfg2_launches.md (`--profile step`) and
+# profiles/conv_sc_large_cu8_launches.md (`--profile ops --large-cells 8`, 91 514 edges); re-captured whenever the
+# kernels change.
+NCU_TRAFFIC_STEP = {'conv_tp[1]': (27.5e6 + 30.9e6, 'ncu launch list of --profile step (profiles/ef_step_cfg2_launches.md)'),
+                    'conv_tp[0]': (11.2e6 + 12.6e6, 'ncu launch list of --profile step (profiles/ef_step_cfg2_launches.md)')}
+CU8_EDGES = 91514
+NCU_TRAFFIC_CU8 = {'conv_tp[1]': (904.2e6 + 2730.3e6, 'ncu launch list of --profile ops --large-cells 8 '
+                                                    '(profiles/conv_sc_large_cu8_launches.md)'),
+                   'conv_tp[0]': (208.1e6 + 380.7e6, 'ncu launch list of --profile ops --large-cells 8 '
+                                                   '(profiles/conv_sc_large_cu8_launches.md)')}
+
 
 def large_cases(dev, cells=LARGE_CELLS):
     """configs[4]'s architecture (128x0e+128x1o+128x2e, l_max 3, correlation 3) on a bulk fcc Cu supercell of
@@ -471,18 +483,23 @@ def main():
     ops = time_cases(step_cases(model, batch), a.op_reps, flush)
     hbm, hbm_kind = peaks()
 
-    def conv_roof(o, note):
+    def conv_roof(o, note, traffic=None):
         b = o['fwd_bytes'] + o['bwd_bytes']
         us = o['fwd_us'] + o['bwd_us']
         ach = b / (us * 1e-6) / 1e9
-        return {'kernel': f"{o['op']} fwd+bwd (mmk_conv_fwd_kernel + mmk_conv_bwd_kernel), N={o['N']} E={o['E']}",
-                'bound': 'hbm', 'achieved': round(ach, 1), 'peak': hbm, 'peak_kind': hbm_kind, 'unit': 'GB/s',
-                'frac': round(ach / hbm, 4), 'traffic': None, 'algorithmic_bytes_per_launch': b,
-                'us_per_launch': round(us, 2), 'note': note}
+        r = {'kernel': f"{o['op']} fwd+bwd (mmk_conv_fwd_kernel + mmk_conv_bwd_kernel), N={o['N']} E={o['E']}",
+             'bound': 'hbm', 'achieved': round(ach, 1), 'peak': hbm, 'peak_kind': hbm_kind, 'unit': 'GB/s',
+             'frac': round(ach / hbm, 4), 'traffic': None, 'algorithmic_bytes_per_launch': b,
+             'us_per_launch': round(us, 2), 'note': note}
+        if traffic is not None:
+            r.update(traffic=int(traffic[0]), traffic_source=traffic[1],
+                     traffic_over_algorithmic=round(traffic[0] / b, 3))
+        return r
 
     dom = max((o for o in ops if o['kind'] == 'conv'), key=lambda o: o['fwd_us'] + o['bwd_us'])
     roofline = conv_roof(dom, 'dominant kernel of the timed E+F step; its data fits in L2, so it is latency-bound '
-                              '(cold: L2 flushed before the launch)')
+                              '(cold: L2 flushed before the launch)',
+                         traffic=NCU_TRAFFIC_STEP.get(dom['op']))
     large, roof_large, fp32 = None, None, None
     if not a.no_large and rank == 0:
         cases, info = large_cases(dev, a.large_cells)
@@ -491,7 +508,10 @@ def main():
         large = dict(info, ops=large_ops, clocks=clk_large.summary())
         del cases
         big = max((o for o in large['ops'] if o['kind'] == 'conv'), key=lambda o: o['fwd_us'] + o['bwd_us'])
-        roof_large = conv_roof(big, 'inputs far larger than L2 (bulk Cu, configs[4] architecture)')
+        tr = NCU_TRAFFIC_CU8.get(big['op'].split()[0])
+        if tr is not None:                          # per-launch bytes of the Cu 8^3 capture, scaled by the edge count
+            tr = (tr[0] * big['E'] / CU8_EDGES, tr[1] + f' x {big["E"] / CU8_EDGES:.2f} (edges)')
+        roof_large = conv_roof(big, 'inputs far larger than L2 (bulk Cu, configs[4] architecture)', traffic=tr)
         fp32 = fp32_peak(dev)
         for o in large['ops'] + ops:
             if o['kind'] == 'sc':
