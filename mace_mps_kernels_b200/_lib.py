@@ -90,7 +90,7 @@ def check(code):
 
 # kernels each entry point launches (bench.py reports the count issued inside its timed region)
 KERNELS_PER_CALL = {'mmk_conv_fwd': 1, 'mmk_conv_bwd': 1, 'mmk_sc_fwd': 1, 'mmk_sc_bwd': 1, 'mmk_csr_build': 4,
-                    'mmk_csr_build_noalloc': 4, 'mmk_elem_index': 1, 'mmk_elem_groups': 4}
+                    'mmk_csr_build_noalloc': 4, 'mmk_elem_index': 1, 'mmk_elem_groups': 3}
 LAUNCHES = collections.Counter()
 
 

@@ -128,6 +128,20 @@ def test_csr_matches_stable_argsort(cuda, N, E, seed):
     assert np.array_equal(eids.cpu().numpy(), e0)
 
 
+@pytest.mark.parametrize('N,n_elem,seed', [(5, 4, 0), (1000, 1, 1), (70000, 3, 2), (257, 89, 3)])
+def test_elem_groups_match_stable_argsort(cuda, N, n_elem, seed):
+    """Nodes grouped by element = a stable argsort of the element index (long segments: one element can hold every
+    node)."""
+    from mace_mps_kernels_b200.symmetric import element_groups
+    rng = np.random.default_rng(seed)
+    e = rng.integers(0, n_elem, N) if seed != 2 else np.where(rng.random(N) < 0.97, 0, rng.integers(0, n_elem, N))
+    attrs = torch.nn.functional.one_hot(torch.from_numpy(e), n_elem).float().to(cuda)
+    elem, erow, perm = element_groups(attrs)
+    assert np.array_equal(elem.cpu().numpy(), e)
+    assert np.array_equal(erow.cpu().numpy(), np.concatenate([[0], np.cumsum(np.bincount(e, minlength=n_elem))]))
+    assert np.array_equal(perm.cpu().numpy(), np.argsort(e, kind='stable'))
+
+
 def test_csr_flags_out_of_range(cuda):
     from mace_mps_kernels_b200 import _lib
     idx = torch.tensor([0, 5, 1, -1, 2], device=cuda)
