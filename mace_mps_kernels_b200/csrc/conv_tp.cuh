@@ -93,6 +93,9 @@ __device__ __forceinline__ bool mbar_wait(u64 *bar, u32 parity) {
     }
     return true;
 }
+// Before a consumer warp releases a ring stage: the producer's next TMA copy writes the stage through the async proxy,
+// and only a proxy fence orders those writes after this warp's generic-proxy reads of the stage.
+__device__ __forceinline__ void release_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, u32 bytes, u64 *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_addr(dst)),
@@ -314,6 +317,7 @@ __device__ __forceinline__ void fwd_consume(const float *smem, u64 *full, u64 *e
                 fwd_load_w<H>(stage, u, w[q]);
                 load_x_s(stage + W_DIM, u, xs[q]);
             }
+            release_fence();
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
 #pragma unroll
@@ -458,6 +462,7 @@ __device__ __forceinline__ void bwd_consume(const float *smem, u64 *full, u64 *e
                     if (lane == 0) arrived[st] = 0;
                 }
             }
+            release_fence();
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
         }

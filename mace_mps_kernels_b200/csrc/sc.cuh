@@ -91,6 +91,11 @@ __device__ __forceinline__ bool group_of(long long g, const int *__restrict__ er
     return false;
 }
 
+// Before a consumer warp hands a stage back to the producer: the producer's next TMA copy writes the stage through
+// the async proxy, and without a proxy fence those writes are not ordered after this warp's generic-proxy reads of
+// the stage (observed on B200: a warp still reading late rows of a column saw the next unit's coefficients).
+__device__ __forceinline__ void release_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // shared memory: ring [STAGES][SC_CC][RP] floats | full[STAGES] | empty[STAGES]
 struct Smem {
     float *ring;
@@ -198,6 +203,7 @@ mmk_sc_fwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, con
             return;
         }
         if (un.c < CH) sc_fwd_body(s.ring + ((size_t)st * SC_CC + j) * RP, xv, acc);   // warp-uniform
+        release_fence();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.empty[st]);
         if (active) sc_fwd_store(acc, un.node, out, un.c);
@@ -241,6 +247,7 @@ mmk_sc_bwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, con
             return;
         }
         if (un.c < CH) sc_bwd_body(s.ring + ((size_t)st * SC_CC + j) * RP, xv, gv, d);   // warp-uniform
+        release_fence();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.empty[st]);
         if (active) store_feat(gx + (un.node * CH + un.c) * NELL, d);
