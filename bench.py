@@ -376,8 +376,8 @@ def main():
 
     torch.manual_seed(0)
     model = standin.make_model(HIDDEN, LMAX, CORR, seed=0, elements=standin.ELEMENTS_PTCOH).to(dev)
-    rep = patch_model(model, verbose=False)
-    assert len(rep['patched']) == 4, rep
+    rep = patch_model(model, verbose=False, edge_features=True)
+    assert len(rep['patched']) == 6, rep
     st, host_batch = workload(rank)
     n_atoms, n_edges = len(st), int(host_batch['edge_index'].shape[1])
     batch = standin.to_device(host_batch, dev)

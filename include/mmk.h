@@ -190,6 +190,33 @@ MMK_API int mmk_sc_fwd(const mmk_sc_layer *layer, const float *x, const int32_t 
 MMK_API int mmk_sc_bwd(const mmk_sc_layer *layer, const float *x, const int32_t *perm, const int32_t *erow, int n_elem,
                        const float *T, const float *grad_out, float *gx, int64_t n_nodes, void *stream);
 
+/* ------------------------------------------------------------------------------------------------------------------
+ * edge geometry (no counterpart in the reference, which leaves MACE's spherical harmonics and radial embedding to
+ * e3nn / PyTorch): the per-edge inputs of the convolution, one thread per edge
+ * ---------------------------------------------------------------------------------------------------------------- */
+
+/* Y[E, (lmax+1)^2] = real spherical harmonics of vectors[E, 3] normalised to unit length ('component' normalisation,
+ * l = 0..lmax <= 3, e3nn's component order m = -l..l), as MACE's o3.SphericalHarmonics(normalize=True). */
+MMK_API int mmk_sh_fwd(const float *vectors, int64_t n_edges, int lmax, float *Y, void *stream);
+/* grad_vectors[E, 3] = d(sum Y * grad_Y)/d vectors. */
+MMK_API int mmk_sh_bwd(const float *vectors, const float *grad_Y, int64_t n_edges, int lmax, float *grad_vectors,
+                       void *stream);
+
+/* MACE's radial embedding: out[e, n] = prefactor * sin(w[n] r) / r * env(r), env = the polynomial cutoff of order p
+ * (1 - (p+1)(p+2)/2 u^p + p(p+2) u^(p+1) - p(p+1)/2 u^(p+2), u = r / r_max, 0 beyond r_max); w, prefactor, r_max, p
+ * are the model's BesselBasis / PolynomialCutoff constants (w: host array of n_bessel floats). */
+typedef struct mmk_radial_desc {
+    int n_bessel;            /* 1..16 */
+    const float *w;          /* [n_bessel] Bessel frequencies (host memory) */
+    float prefactor;         /* sqrt(2 / r_max) */
+    float r_max;
+    float p;
+} mmk_radial_desc;
+MMK_API int mmk_radial_fwd(const mmk_radial_desc *desc, const float *lengths, int64_t n_edges, float *out, void *stream);
+/* grad_lengths[E] = d(sum out * grad_out)/d lengths */
+MMK_API int mmk_radial_bwd(const mmk_radial_desc *desc, const float *lengths, const float *grad_out, int64_t n_edges,
+                           float *grad_lengths, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

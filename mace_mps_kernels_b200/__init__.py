@@ -8,8 +8,10 @@ Replaces, where supported (same contract as Yike-Ye/mace-mps-kernels, reference 
   * each interaction block's convolution (gather -> channel-wise tensor product -> scatter-sum) via MACE's own
     ``conv_fusion`` hook,
   * each product block's symmetric contraction.
-Everything else stays on the original PyTorch path.  Inference only: the backward pass is first order (energies,
-forces, stress, relaxations, MD); double backward raises an error.
+Everything else stays on the original PyTorch path, except, with ``edge_features=True`` (an extension beyond the
+reference), the model's spherical harmonics and radial embedding, which then run as one CUDA kernel each way.
+Inference only: the backward pass is first order (energies, forces, stress, relaxations, MD); double backward raises
+an error.
 """
 import inspect
 import warnings
@@ -17,10 +19,12 @@ import warnings
 import torch
 
 from .conv import CudaConvTP, MetalConvTP, conv_supported
+from .edge import CudaRadialEmbedding, CudaSphericalHarmonics, radial_supported, sh_supported
 from .symmetric import CudaSymmetricContraction, MetalSymmetricContraction, sc_supported
 
 __version__ = '0.1.0'
-__all__ = ['patch_model', 'CudaConvTP', 'CudaSymmetricContraction', 'MetalConvTP', 'MetalSymmetricContraction']
+__all__ = ['patch_model', 'CudaConvTP', 'CudaSymmetricContraction', 'MetalConvTP', 'MetalSymmetricContraction',
+           'CudaSphericalHarmonics', 'CudaRadialEmbedding']
 
 
 def _block_has_conv_fusion(blk):
@@ -30,12 +34,14 @@ def _block_has_conv_fusion(blk):
         return False
 
 
-def patch_model(model, conv=True, symmetric=True, verbose=True):
+def patch_model(model, conv=True, symmetric=True, verbose=True, edge_features=False):
     """Swap supported ops for CUDA kernels, in place.  Returns {'patched': [...], 'skipped': [(name, reason)]}.
 
     Mirrors reference ``__init__.py:34-79``: a float32 model on the accelerator (here CUDA), interaction blocks that
     expose MACE's ``conv_fusion`` path, product blocks without the cuequivariance layout; already-patched blocks are
-    left alone (idempotent) and every skip is reported (and warned about when ``verbose``)."""
+    left alone (idempotent) and every skip is reported (and warned about when ``verbose``).  ``edge_features=True``
+    also swaps ``spherical_harmonics`` and ``radial_embedding`` (not in the reference; off by default so the default
+    report is the reference's)."""
     p0 = next(model.parameters())
     dev = p0.device
     if dev.type != 'cuda':
@@ -77,6 +83,18 @@ def patch_model(model, conv=True, symmetric=True, verbose=True):
                     skipped.append((name, why))
                     continue
                 prod.symmetric_contractions = CudaSymmetricContraction(sc, device=dev)
+                patched.append(name)
+        if edge_features:
+            for name, cls, check in (('spherical_harmonics', CudaSphericalHarmonics, sh_supported),
+                                     ('radial_embedding', CudaRadialEmbedding, radial_supported)):
+                mod = getattr(model, name, None)
+                if isinstance(mod, cls):
+                    continue
+                ok, why = check(mod)
+                if not ok:
+                    skipped.append((name, why))
+                    continue
+                setattr(model, name, cls(mod))
                 patched.append(name)
     if verbose:
         for name, why in skipped:

@@ -27,6 +27,11 @@ class ConvDesc(ctypes.Structure):
                 ('term_ins', _ip), ('term_a', _ip), ('term_b', _ip), ('term_m', _ip), ('term_c', _dp)]
 
 
+class RadialDesc(ctypes.Structure):
+    _fields_ = [('n_bessel', _i), ('w', ctypes.POINTER(ctypes.c_float)), ('prefactor', ctypes.c_float),
+                ('r_max', ctypes.c_float), ('p', ctypes.c_float)]
+
+
 class SCDesc(ctypes.Structure):
     _fields_ = [('C', _i), ('n_ell', _i), ('n_rows', _i), ('n_blocks', _i), ('block_M', _ip), ('block_nterms', _ip),
                 ('max_degree', _i), ('term_degree', _ip), ('term_idx', _ip), ('term_row', _ip)]
@@ -51,6 +56,10 @@ SIGNATURES = {
     'mmk_sc_layer_destroy': (_i, [_p]),
     'mmk_sc_layer_dims': (_i, [_p, _ip, _ip, _ip, _ip]),
     'mmk_sc_compile_check': (_i, [ctypes.POINTER(SCDesc)]),
+    'mmk_sh_fwd': (_i, [_p, _i64, _i, _p, _p]),
+    'mmk_sh_bwd': (_i, [_p, _p, _i64, _i, _p, _p]),
+    'mmk_radial_fwd': (_i, [ctypes.POINTER(RadialDesc), _p, _i64, _p, _p]),
+    'mmk_radial_bwd': (_i, [ctypes.POINTER(RadialDesc), _p, _p, _i64, _p, _p]),
     'mmk_sc_source': (_i, [ctypes.POINTER(SCDesc), ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     'mmk_sc_layer_status': (_i, [_p, _ip, _i]),
     'mmk_elem_index': (_i, [_p, _i64, _i, _p, _p]),
@@ -90,7 +99,8 @@ def check(code):
 
 # kernels each entry point launches (bench.py reports the count issued inside its timed region)
 KERNELS_PER_CALL = {'mmk_conv_fwd': 1, 'mmk_conv_bwd': 1, 'mmk_sc_fwd': 1, 'mmk_sc_bwd': 1, 'mmk_csr_build': 4,
-                    'mmk_csr_build_noalloc': 4, 'mmk_elem_index': 1, 'mmk_elem_groups': 3}
+                    'mmk_csr_build_noalloc': 4, 'mmk_elem_index': 1, 'mmk_elem_groups': 3,
+                    'mmk_sh_fwd': 1, 'mmk_sh_bwd': 1, 'mmk_radial_fwd': 1, 'mmk_radial_bwd': 1}
 LAUNCHES = collections.Counter()
 
 

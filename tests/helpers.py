@@ -86,13 +86,13 @@ def energy_forces(model, structure, device, R=None):
     return float(out['energy'].detach().sum()), out['forces'].detach().cpu().double().numpy()
 
 
-def pair(config, device):
+def pair(config, device, **patch_kw):
     """(reference model, patched deep copy, report) for a CONFIGS entry."""
     from mace_mps_kernels_b200 import patch_model
     hidden, lmax, corr, seed = CONFIGS[config]
     ref = make_model(hidden, lmax, corr, seed).to(device)
     met = copy.deepcopy(ref)
-    report = patch_model(met, verbose=False)
+    report = patch_model(met, verbose=False, **patch_kw)
     return ref, met, report
 
 
