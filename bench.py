@@ -322,7 +322,7 @@ def cpu_baseline(n_steps_cap=5, budget_s=20.0):
     """Unpatched (e3nn-path) stand-in model on the host cores: E+F atom-steps/s on this rank's structure."""
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    model = standin.make_model(HIDDEN, LMAX, CORR, seed=0, elements=standin.ELEMENTS_PTCOH)
+    model = standin.make_model(HIDDEN, LMAX, CORR, seed=0, elements=standin.ELEMENTS_PTCOH).requires_grad_(False)
     st, batch = workload(0)
     e_and_f(model, batch)                       # warm-up (allocations, caches)
     times = []
@@ -376,8 +376,9 @@ def main():
 
     torch.manual_seed(0)
     model = standin.make_model(HIDDEN, LMAX, CORR, seed=0, elements=standin.ELEMENTS_PTCOH).to(dev)
-    rep = patch_model(model, verbose=False, edge_features=True)
-    assert len(rep['patched']) == 6, rep
+    model.requires_grad_(False)                 # inference: frozen weights, as MACE's calculators run the model
+    rep = patch_model(model, verbose=False, edge_features=True, linears=True)
+    assert not rep['skipped'] and len(rep['patched']) >= 6, rep
     st, host_batch = workload(rank)
     n_atoms, n_edges = len(st), int(host_batch['edge_index'].shape[1])
     batch = standin.to_device(host_batch, dev)
@@ -628,7 +629,7 @@ def reference_arm(a, rank, world):
         return
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    model = standin.make_model(HIDDEN, LMAX, CORR, seed=0, elements=standin.ELEMENTS_PTCOH)
+    model = standin.make_model(HIDDEN, LMAX, CORR, seed=0, elements=standin.ELEMENTS_PTCOH).requires_grad_(False)
     st, batch = workload(0)
     for _ in range(a.warmup):
         e_and_f(model, batch)

@@ -19,12 +19,13 @@ import warnings
 import torch
 
 from .conv import CudaConvTP, MetalConvTP, conv_supported
+from .dense import CudaLinear, CudaSkipTP
 from .edge import CudaRadialEmbedding, CudaSphericalHarmonics, radial_supported, sh_supported
 from .symmetric import CudaSymmetricContraction, MetalSymmetricContraction, sc_supported
 
 __version__ = '0.1.0'
 __all__ = ['patch_model', 'CudaConvTP', 'CudaSymmetricContraction', 'MetalConvTP', 'MetalSymmetricContraction',
-           'CudaSphericalHarmonics', 'CudaRadialEmbedding']
+           'CudaSphericalHarmonics', 'CudaRadialEmbedding', 'CudaLinear', 'CudaSkipTP']
 
 
 def _block_has_conv_fusion(blk):
@@ -34,14 +35,15 @@ def _block_has_conv_fusion(blk):
         return False
 
 
-def patch_model(model, conv=True, symmetric=True, verbose=True, edge_features=False):
+def patch_model(model, conv=True, symmetric=True, verbose=True, edge_features=False, linears=False):
     """Swap supported ops for CUDA kernels, in place.  Returns {'patched': [...], 'skipped': [(name, reason)]}.
 
     Mirrors reference ``__init__.py:34-79``: a float32 model on the accelerator (here CUDA), interaction blocks that
     expose MACE's ``conv_fusion`` path, product blocks without the cuequivariance layout; already-patched blocks are
-    left alone (idempotent) and every skip is reported (and warned about when ``verbose``).  ``edge_features=True``
-    also swaps ``spherical_harmonics`` and ``radial_embedding`` (not in the reference; off by default so the default
-    report is the reference's)."""
+    left alone (idempotent) and every skip is reported (and warned about when ``verbose``).  Extensions beyond the
+    reference, off by default so that the default report is the reference's: ``edge_features=True`` also swaps
+    ``spherical_harmonics`` and ``radial_embedding``; ``linears=True`` swaps every equivariant linear layer and the
+    element-indexed skip connections (frozen weights only, see ``dense.py``)."""
     p0 = next(model.parameters())
     dev = p0.device
     if dev.type != 'cuda':
@@ -96,6 +98,23 @@ def patch_model(model, conv=True, symmetric=True, verbose=True, edge_features=Fa
                     continue
                 setattr(model, name, cls(mod))
                 patched.append(name)
+        if linears:
+            from .dense import CudaLinear, CudaSkipTP, linear_supported, skip_supported
+            for pname, parent in list(model.named_modules()):
+                for cname, child in list(parent.named_children()):
+                    kind = type(child).__name__
+                    if kind == 'Linear' and hasattr(child, 'paths'):
+                        cls, (ok, why) = CudaLinear, linear_supported(child)
+                    elif kind == 'FullyConnectedTensorProduct' and hasattr(child, 'paths'):
+                        cls, (ok, why) = CudaSkipTP, skip_supported(child)
+                    else:
+                        continue
+                    full = f'{pname}.{cname}' if pname else cname
+                    if not ok:
+                        skipped.append((full, why))
+                        continue
+                    setattr(parent, cname, cls(child))
+                    patched.append(full)
     if verbose:
         for name, why in skipped:
             warnings.warn(f'mace-b200-kernels: kept e3nn for {name}: {why}')

@@ -1,0 +1,149 @@
+"""MACE's equivariant linear layers on B200: ``o3.Linear`` and the element-indexed skip connection
+(``FullyConnectedTensorProduct`` of the node features with the one-hot node attributes), one CUDA launch each way
+(C ABI ``mmk_block_linear``) instead of a slice / scale / einsum / add chain per path.
+
+A layer is a list of paths (input block ii -> output block io of the same irrep, weight W [mul_in, mul_out] scaled
+by 1/sqrt(fan_in)); the forward applies them all at once, the backward (gradient w.r.t. the input only) applies the
+transposed paths.  With one-hot node attributes the skip connection is a linear map whose weight is selected by the
+node's element, W_e = W[:, e, :]; the kernel works on nodes grouped by element (the symmetric contraction's groups).
+
+Inference only: the weights must be frozen (``requires_grad`` False, as MACE's calculators set them), the backward is
+first order, double backward raises.  ``patch_model(model, linears=True)`` swaps every supported layer.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib
+from .conv import DOUBLE_BACKWARD_MSG
+
+
+def _blocks(irreps):
+    """[(offset, mul, dim)] of an Irreps (mul_ir layout)."""
+    out, off = [], 0
+    for mul, ir in irreps:
+        out.append((off, mul, ir.dim))
+        off += mul * ir.dim
+    return out, off
+
+
+def linear_supported(mod):
+    """(ok, reason) for an equivariant linear with explicit per-path weights (the layout of this repository's MACE)."""
+    if not hasattr(mod, 'paths') or not hasattr(mod, 'weight') or not (hasattr(mod, 'irreps_in') or
+                                                                       hasattr(mod, 'irreps_in1')):
+        return False, 'not a per-path equivariant linear'
+    if any(p.requires_grad for p in mod.parameters()):
+        return False, 'weights require grad (training): frozen weights only'
+    return True, ''
+
+
+def skip_supported(mod):
+    ok, why = linear_supported(mod)
+    if not ok:
+        return ok, why
+    if not hasattr(mod, 'irreps_in2') or any(ir.l != 0 for _, ir in mod.irreps_in2):
+        return False, 'second operand must be scalar node attributes'
+    return True, ''
+
+
+class _Tables:
+    """Device path tables of one direction: int32 blocks [n_out_blocks, 5], paths [n_paths, 3], packed weights."""
+
+    def __init__(self, out_blocks, path_list, device):
+        blocks, paths, w = [], [], []
+        w_off = 0
+        for b, (off, mul, d) in enumerate(out_blocks):
+            mine = [p for p in path_list if p[1] == b]
+            blocks.append([off, mul, d, len(paths), len(mine)])
+            for src_off, _, W in mine:                 # W: [n_elem, mul_in, mul_out] float32
+                paths.append([src_off, W.shape[1], w_off])
+                w.append(W.reshape(-1))
+                w_off += W.size
+        self.n_blocks = len(blocks)
+        self.max_d = max(d for _, _, d in out_blocks)
+        self.blocks = torch.tensor(np.asarray(blocks, np.int32).reshape(-1, 5), device=device)
+        self.paths = torch.tensor(np.asarray(paths, np.int32).reshape(-1, 3), device=device)
+        wv = np.concatenate(w) if w else np.zeros(1, np.float32)
+        self.w = torch.tensor(wv.astype(np.float32), device=device)
+        if w_off >= 2 ** 31:
+            raise ValueError('layer too large')
+
+
+class _BlockLinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, op, groups):
+        x = x.contiguous()
+        if x.dtype != torch.float32 or not x.is_cuda:
+            raise TypeError('input must be a float32 CUDA tensor')
+        N = x.shape[0]
+        out = torch.empty(N, op.out_dim, device=x.device, dtype=torch.float32)
+        op._launch(op.fwd, x, op.in_dim, out, op.out_dim, groups)
+        ctx.op, ctx.groups = op, groups
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        if torch.is_grad_enabled():
+            raise RuntimeError(DOUBLE_BACKWARD_MSG)
+        op = ctx.op
+        g = g.contiguous()
+        gx = torch.empty(g.shape[0], op.in_dim, device=g.device, dtype=torch.float32)
+        op._launch(op.bwd, g, op.out_dim, gx, op.in_dim, ctx.groups)
+        return gx, None, None
+
+
+class _BlockLinearBase(torch.nn.Module):
+    def _build(self, in_irreps, out_irreps, path_list, device):
+        """path_list: (ii, io, W [n_elem, mul_in, mul_out] float32 numpy, already scaled)."""
+        ib, self.in_dim = _blocks(in_irreps)
+        ob, self.out_dim = _blocks(out_irreps)
+        self.fwd = _Tables(ob, [(ib[ii][0], io, W) for ii, io, W in path_list], device)
+        self.bwd = _Tables(ib, [(ob[io][0], ii, np.ascontiguousarray(W.transpose(0, 2, 1)))
+                                for ii, io, W in path_list], device)
+
+    def _launch(self, t, x, ldx, out, ldo, groups):
+        perm, erow, n_elem = groups if groups is not None else (None, None, 1)
+        _lib.call('mmk_block_linear', _lib.ptr(x), ldx, _lib.ptr(out), ldo, _lib.ptr(t.blocks), t.n_blocks,
+                  _lib.ptr(t.paths), _lib.ptr(t.w), t.max_d, _lib.ptr(perm), _lib.ptr(erow), n_elem, x.shape[0],
+                  _lib.stream_of(x))
+
+
+class CudaLinear(_BlockLinearBase):
+    """Drop-in for the equivariant ``o3.Linear`` (frozen weights): forward(x[N, in_dim]) -> [N, out_dim]."""
+
+    def __init__(self, lin):
+        super().__init__()
+        ok, why = linear_supported(lin)
+        if not ok:
+            raise ValueError(why)
+        self.irreps_in, self.irreps_out = lin.irreps_in, lin.irreps_out
+        dev = next(lin.parameters()).device
+        path_list = [(ii, io, (w.detach() * s).float().cpu().numpy()[None]) for (ii, io, s), w in
+                     zip(lin.paths, lin.weight)]
+        self._build(lin.irreps_in, lin.irreps_out, path_list, dev)
+
+    def forward(self, x):
+        return _BlockLinearFn.apply(x, self, None)
+
+
+class CudaSkipTP(_BlockLinearBase):
+    """Drop-in for MACE's skip connection ``FullyConnectedTensorProduct(node_feats, node_attrs)`` with one-hot node
+    attributes (frozen weights): forward(x1[N, in_dim], node_attrs[N, n_elem]) -> [N, out_dim]."""
+
+    def __init__(self, tp):
+        super().__init__()
+        ok, why = skip_supported(tp)
+        if not ok:
+            raise ValueError(why)
+        self.irreps_in1, self.irreps_in2, self.irreps_out = tp.irreps_in1, tp.irreps_in2, tp.irreps_out
+        self.n_elem = tp.irreps_in2.dim
+        dev = next(tp.parameters()).device
+        path_list = [(ii, io, (w.detach() * s).float().cpu().numpy().transpose(1, 0, 2).copy()) for (ii, io, s), w
+                     in zip(tp.paths, tp.weight)]                        # [mul_in, n_elem, mul_out] -> [e, u, w]
+        self._build(tp.irreps_in1, tp.irreps_out, path_list, dev)
+
+    def forward(self, x1, node_attrs):
+        from .symmetric import element_groups
+        _, erow, perm = element_groups(node_attrs)
+        return _BlockLinearFn.apply(x1, self, (perm, erow, self.n_elem))

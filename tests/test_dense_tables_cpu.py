@@ -1,0 +1,65 @@
+"""Path tables of the block-linear layers (dense.py), evaluated with numpy exactly as the CUDA kernel reads them, against
+the model's own equivariant linear / skip-connection modules and their input gradients (CPU, no GPU needed)."""
+import numpy as np
+import torch
+
+from mace_mps_kernels_b200.dense import CudaLinear, CudaSkipTP
+from mace_mps_kernels_b200.standin import o3
+
+
+def _apply(t, x, elem=None):
+    """out = what mmk_block_linear computes from the tables t (blocks, paths, packed weights)."""
+    blocks, paths, w = t.blocks.numpy(), t.paths.numpy(), t.w.numpy()
+    N = x.shape[0]
+    e = np.zeros(N, int) if elem is None else elem
+    dim = max(b[0] + b[1] * b[2] for b in blocks)
+    out = np.full((N, dim), np.nan)
+    for dst_off, mul_out, d, p0, n_p in blocks:
+        acc = np.zeros((N, mul_out, d))
+        for src_off, mul_in, w_off in paths[p0:p0 + n_p]:
+            W = w[w_off:w_off + (e.max() + 1) * mul_in * mul_out].reshape(-1, mul_in, mul_out)[e]   # [N, u, v]
+            xb = x[:, src_off:src_off + mul_in * d].reshape(N, mul_in, d)
+            acc += np.einsum('nud,nuv->nvd', xb, W)
+        out[:, dst_off:dst_off + mul_out * d] = acc.reshape(N, -1)
+    return out
+
+
+def _frozen(m):
+    for p in m.parameters():
+        p.requires_grad_(False)
+    return m
+
+
+def test_linear_tables_match_module():
+    torch.manual_seed(0)
+    lin = _frozen(o3.Linear(o3.Irreps('8x0e+4x1o+8x0e+3x2e+2x1o'), o3.Irreps('5x0e+6x1o+2x2e+3x3o')))
+    op = CudaLinear(lin)
+    x = torch.randn(7, lin.irreps_in.dim, dtype=torch.float32)
+    ref = lin(x).numpy()
+    out = _apply(op.fwd, x.numpy())
+    assert np.abs(out - ref).max() < 1e-5 * np.abs(ref).max()          # 3x3o has no source: zeros
+    xr = x.clone().requires_grad_(True)
+    g = torch.randn(7, lin.irreps_out.dim)
+    (gx,) = torch.autograd.grad(lin(xr), xr, g)
+    gout = _apply(op.bwd, g.numpy())
+    assert np.abs(gout - gx.numpy()).max() < 1e-5 * np.abs(gx.numpy()).max()
+
+
+def test_skip_tables_match_module():
+    torch.manual_seed(1)
+    n_elem = 4
+    tp = _frozen(o3.FullyConnectedTensorProduct(o3.Irreps('16x0e+8x1o'), o3.Irreps(f'{n_elem}x0e'),
+                                                o3.Irreps('16x0e+8x1o+4x2e')))
+    op = CudaSkipTP(tp)
+    N = 9
+    x1 = torch.randn(N, tp.irreps_in1.dim)
+    elem = np.arange(N) % n_elem
+    attrs = torch.nn.functional.one_hot(torch.from_numpy(elem), n_elem).float()
+    ref = tp(x1, attrs).numpy()
+    out = _apply(op.fwd, x1.numpy(), elem)
+    assert np.abs(out - ref).max() < 1e-5 * np.abs(ref).max()
+    xr = x1.clone().requires_grad_(True)
+    g = torch.randn(N, tp.irreps_out.dim)
+    (gx,) = torch.autograd.grad(tp(xr, attrs), xr, g)
+    gout = _apply(op.bwd, g.numpy(), elem)
+    assert np.abs(gout - gx.numpy()).max() < 1e-5 * np.abs(gx.numpy()).max()

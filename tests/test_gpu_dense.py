@@ -1,0 +1,90 @@
+"""Block-linear kernels (equivariant linears and element-indexed skip connections) against the model's own modules on
+the GPU, and the whole model with every extension patched (frozen weights) against the unpatched model."""
+import copy
+
+import numpy as np
+import pytest
+import torch
+
+import helpers
+from helpers import E_ABS, E_TOL, F_ABS, F_TOL
+
+pytestmark = pytest.mark.gpu
+
+
+def _frozen(m):
+    for p in m.parameters():
+        p.requires_grad_(False)
+    return m
+
+
+@pytest.mark.parametrize('irr_in,irr_out,N', [
+    ('128x0e+128x1o', '128x0e+128x1o', 168),
+    ('128x0e+128x1o+128x0e+128x2e+128x1o+128x3o', '128x0e+128x1o+128x2e+128x3o', 5003),
+    ('16x0e', '1x0e', 70),
+    ('40x0e+24x1o', '200x0e+24x1o+8x2e', 1000),
+])
+def test_linear_matches_module(cuda, irr_in, irr_out, N):
+    from mace_mps_kernels_b200.dense import CudaLinear
+    from mace_mps_kernels_b200.standin import o3
+    torch.manual_seed(0)
+    lin = _frozen(o3.Linear(o3.Irreps(irr_in), o3.Irreps(irr_out))).to(cuda)
+    op = CudaLinear(lin)
+    x = torch.randn(N, lin.irreps_in.dim, device=cuda, requires_grad=True)
+    out = op(x)
+    lin64 = copy.deepcopy(lin).double().cpu()
+    x64 = x.detach().double().cpu().requires_grad_(True)
+    ref = lin64(x64)
+    assert (out.double().cpu() - ref.detach()).abs().max().item() < 2e-5 * ref.abs().max().item()
+    g = torch.randn_like(out)
+    (gx,) = torch.autograd.grad(out, x, g)
+    (gx64,) = torch.autograd.grad(ref, x64, g.double().cpu())
+    assert (gx.double().cpu() - gx64).abs().max().item() < 2e-5 * gx64.abs().max().item()
+    assert torch.equal(op(x.detach()), out.detach())
+
+
+@pytest.mark.parametrize('N,n_elem', [(168, 4), (3001, 3), (5, 89)])
+def test_skip_tp_matches_module(cuda, N, n_elem):
+    from mace_mps_kernels_b200.dense import CudaSkipTP
+    from mace_mps_kernels_b200.standin import o3
+    torch.manual_seed(1)
+    tp = _frozen(o3.FullyConnectedTensorProduct(o3.Irreps('128x0e+128x1o'), o3.Irreps(f'{n_elem}x0e'),
+                                                o3.Irreps('128x0e+128x1o+128x2e'))).to(cuda)
+    op = CudaSkipTP(tp)
+    elem = torch.from_numpy(np.random.default_rng(N).integers(0, n_elem, N))
+    attrs = torch.nn.functional.one_hot(elem, n_elem).float().to(cuda)
+    x = torch.randn(N, tp.irreps_in1.dim, device=cuda, requires_grad=True)
+    out = op(x, attrs)
+    tp64 = copy.deepcopy(tp).double().cpu()
+    x64 = x.detach().double().cpu().requires_grad_(True)
+    ref = tp64(x64, attrs.double().cpu())
+    assert (out.double().cpu() - ref.detach()).abs().max().item() < 2e-5 * ref.abs().max().item()
+    g = torch.randn_like(out)
+    (gx,) = torch.autograd.grad(out, x, g)
+    (gx64,) = torch.autograd.grad(ref, x64, g.double().cpu())
+    assert (gx.double().cpu() - gx64).abs().max().item() < 2e-5 * gx64.abs().max().item()
+
+
+@pytest.mark.parametrize('config', ['l3_corr3', 'l3_corr3_l2hidden'])
+def test_model_all_extensions_matches_unpatched(cuda, config):
+    from mace_mps_kernels_b200 import patch_model
+    hidden, lmax, corr, seed = helpers.CONFIGS[config]
+    ref = _frozen(helpers.make_model(hidden, lmax, corr, seed).to(cuda))
+    met = copy.deepcopy(ref)
+    report = patch_model(met, verbose=False, edge_features=True, linears=True)
+    assert not report['skipped'], report['skipped']
+    assert 'interactions.0.linear_up' in report['patched'] and 'interactions.1.skip_tp' in report['patched']
+    for s in (0, 1):
+        st = helpers.make_structure(seed=s)
+        E0, F0 = helpers.energy_forces(ref, st, cuda)
+        E1, F1 = helpers.energy_forces(met, st, cuda)
+        dE, dF = abs(E1 - E0), np.abs(F1 - F0).max()
+        assert dE / len(st) < E_TOL and dF / max(np.abs(F0).max(), 1e-3) < F_TOL, (config, s, dE, dF)
+        assert dE <= E_ABS and dF <= F_ABS
+
+
+def test_linears_need_frozen_weights(cuda):
+    from mace_mps_kernels_b200 import patch_model
+    model = helpers.make_model().to(cuda)
+    report = patch_model(model, verbose=False, linears=True)
+    assert any('frozen weights only' in why for _, why in report['skipped'])
