@@ -226,12 +226,13 @@ MMK_API int mmk_radial_bwd(const mmk_radial_desc *desc, const float *lengths, co
  *                                  sum_u x[n, src_off_p + u*d_b + i] * weights[w_off_p + e(n)*mul_in_p*mul_out_b + u*mul_out_b + v]
  * blocks: device int32 [n_blocks][5] = (dst_off, mul_out, d, first path, number of paths); every output block is
  * written (zero when it has no path); paths: device int32 [*][3] = (src_off, mul_in, w_off); rows x[n] / out[n] at
- * n*ldx / n*ldo floats; max_d = the largest d of any block.  Element-indexed weights (MACE's skip connection with
+ * n*ldx / n*ldo floats; max_d / max_mul_out = the largest d / mul_out of any block.  Element-indexed weights (MACE's
+ * skip connection with
  * one-hot node attributes): perm / erow = mmk_elem_groups of the element index, e(n) = the node's element; otherwise
  * perm = erow = NULL, n_elem = 1, e = 0. */
 MMK_API int mmk_block_linear(const float *x, int64_t ldx, float *out, int64_t ldo, const int32_t *blocks, int n_blocks,
-                             const int32_t *paths, const float *weights, int max_d, const int32_t *perm,
-                             const int32_t *erow, int n_elem, int64_t n_nodes, void *stream);
+                             const int32_t *paths, const float *weights, int max_d, int max_mul_out,
+                             const int32_t *perm, const int32_t *erow, int n_elem, int64_t n_nodes, void *stream);
 
 #ifdef __cplusplus
 }

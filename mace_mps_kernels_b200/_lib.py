@@ -60,7 +60,7 @@ SIGNATURES = {
     'mmk_sh_bwd': (_i, [_p, _p, _i64, _i, _p, _p]),
     'mmk_radial_fwd': (_i, [ctypes.POINTER(RadialDesc), _p, _i64, _p, _p]),
     'mmk_radial_bwd': (_i, [ctypes.POINTER(RadialDesc), _p, _p, _i64, _p, _p]),
-    'mmk_block_linear': (_i, [_p, _i64, _p, _i64, _p, _i, _p, _p, _i, _p, _p, _i, _i64, _p]),
+    'mmk_block_linear': (_i, [_p, _i64, _p, _i64, _p, _i, _p, _p, _i, _i, _p, _p, _i, _i64, _p]),
     'mmk_sc_source': (_i, [ctypes.POINTER(SCDesc), ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     'mmk_sc_layer_status': (_i, [_p, _ip, _i]),
     'mmk_elem_index': (_i, [_p, _i64, _i, _p, _p]),

@@ -62,6 +62,7 @@ class _Tables:
                 w_off += W.size
         self.n_blocks = len(blocks)
         self.max_d = max(d for _, _, d in out_blocks)
+        self.max_mul = max(mul for _, mul, _ in out_blocks)
         self.blocks = torch.tensor(np.asarray(blocks, np.int32).reshape(-1, 5), device=device)
         self.paths = torch.tensor(np.asarray(paths, np.int32).reshape(-1, 3), device=device)
         wv = np.concatenate(w) if w else np.zeros(1, np.float32)
@@ -105,7 +106,8 @@ class _BlockLinearBase(torch.nn.Module):
     def _launch(self, t, x, ldx, out, ldo, groups):
         perm, erow, n_elem = groups if groups is not None else (None, None, 1)
         _lib.call('mmk_block_linear', _lib.ptr(x), ldx, _lib.ptr(out), ldo, _lib.ptr(t.blocks), t.n_blocks,
-                  _lib.ptr(t.paths), _lib.ptr(t.w), t.max_d, _lib.ptr(perm), _lib.ptr(erow), n_elem, x.shape[0],
+                  _lib.ptr(t.paths), _lib.ptr(t.w), t.max_d, t.max_mul, _lib.ptr(perm), _lib.ptr(erow), n_elem,
+                  x.shape[0],
                   _lib.stream_of(x))
 
 
