@@ -234,6 +234,15 @@ MMK_API int mmk_block_linear(const float *x, int64_t ldx, float *out, int64_t ld
                              const int32_t *paths, const float *weights, int max_d, int max_mul_out,
                              const int32_t *perm, const int32_t *erow, int n_elem, int64_t n_nodes, void *stream);
 
+/* mmk_block_linear with the activation of an MLP layer (MACE's radial MLP: SiLU times a constant):
+ *   epilogue != 0: zout = the product (pre-activation), out = act_scale * silu(zout)           (forward of a layer)
+ *   prologue != 0: every input element x is multiplied by act_scale * silu'(zin) first          (input-gradient pass)
+ * zout / zin have the layout of out / x.  Not both. */
+MMK_API int mmk_block_linear_act(const float *x, int64_t ldx, float *out, int64_t ldo, const int32_t *blocks,
+                                 int n_blocks, const int32_t *paths, const float *weights, int max_d, int max_mul_out,
+                                 const int32_t *perm, const int32_t *erow, int n_elem, int64_t n_nodes, int epilogue,
+                                 float *zout, int prologue, const float *zin, float act_scale, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -99,7 +99,8 @@ def patch_model(model, conv=True, symmetric=True, verbose=True, edge_features=Fa
                 setattr(model, name, cls(mod))
                 patched.append(name)
         if linears:
-            from .dense import CudaLinear, CudaSkipTP, linear_supported, skip_supported
+            from .dense import (CudaFullyConnectedNet, CudaLinear, CudaSkipTP, linear_supported, mlp_supported,
+                                skip_supported)
             for pname, parent in list(model.named_modules()):
                 for cname, child in list(parent.named_children()):
                     kind = type(child).__name__
@@ -107,6 +108,8 @@ def patch_model(model, conv=True, symmetric=True, verbose=True, edge_features=Fa
                         cls, (ok, why) = CudaLinear, linear_supported(child)
                     elif kind == 'FullyConnectedTensorProduct' and hasattr(child, 'paths'):
                         cls, (ok, why) = CudaSkipTP, skip_supported(child)
+                    elif kind == 'FullyConnectedNet' and hasattr(child, 'hs'):
+                        cls, (ok, why) = CudaFullyConnectedNet, mlp_supported(child)
                     else:
                         continue
                     full = f'{pname}.{cname}' if pname else cname

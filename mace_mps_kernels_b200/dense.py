@@ -7,6 +7,11 @@ by 1/sqrt(fan_in)); the forward applies them all at once, the backward (gradient
 transposed paths.  With one-hot node attributes the skip connection is a linear map whose weight is selected by the
 node's element, W_e = W[:, e, :]; the kernel works on nodes grouped by element (the symmetric contraction's groups).
 
+The radial MLP of an interaction (``FullyConnectedNet``: scalar layers without biases, h <- c * silu(h @ W / sqrt(fan_in))
+except after the last layer) uses the same kernel, one launch per layer each way: the forward stores every hidden
+pre-activation and applies c * silu in the epilogue, the backward applies c * silu'(z) to the incoming gradient as it
+loads it.
+
 Inference only: the weights must be frozen (``requires_grad`` False, as MACE's calculators set them), the backward is
 first order, double backward raises.  ``patch_model(model, linears=True)`` swaps every supported layer.
 """
@@ -149,3 +154,79 @@ class CudaSkipTP(_BlockLinearBase):
         from .symmetric import element_groups
         _, erow, perm = element_groups(node_attrs)
         return _BlockLinearFn.apply(x1, self, (perm, erow, self.n_elem))
+
+
+def mlp_supported(mod):
+    """(ok, reason) for an e3nn-style scalar MLP without biases and with SiLU (MACE's radial MLP)."""
+    ws = getattr(mod, 'weights', None)
+    if ws is None or not hasattr(mod, 'hs') or not hasattr(mod, '_SILU_2MOM'):
+        return False, 'not a bias-free scalar MLP'
+    if getattr(mod, 'act', None) is not torch.nn.functional.silu:
+        return False, 'activation is not SiLU'
+    if any(p.requires_grad for p in mod.parameters()):
+        return False, 'weights require grad (training): frozen weights only'
+    return True, ''
+
+
+class _MLPFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, op):
+        h = x.contiguous()
+        if h.dtype != torch.float32 or not h.is_cuda:
+            raise TypeError('input must be a float32 CUDA tensor')
+        N = h.shape[0]
+        zs = []
+        for i, (fwd, dout) in enumerate(zip(op.fwd, op.dims[1:])):
+            out = torch.empty(N, dout, device=h.device, dtype=torch.float32)
+            if i < len(op.fwd) - 1:
+                z = torch.empty_like(out)
+                op._launch(fwd, h, out, epilogue=z)
+                zs.append(z)
+            else:
+                op._launch(fwd, h, out)
+            h = out
+        ctx.save_for_backward(*zs)
+        ctx.op = op
+        return h
+
+    @staticmethod
+    def backward(ctx, g):
+        if torch.is_grad_enabled():
+            raise RuntimeError(DOUBLE_BACKWARD_MSG)
+        op, zs = ctx.op, ctx.saved_tensors
+        g = g.contiguous()
+        L = len(op.bwd)
+        for i in range(L - 1, -1, -1):
+            gin = torch.empty(g.shape[0], op.dims[i], device=g.device, dtype=torch.float32)
+            # the gradient reaching layer i's output passes through layer i's activation (none after the last layer)
+            op._launch(op.bwd[i], g, gin, prologue=zs[i] if i < L - 1 else None)
+            g = gin
+        return g, None
+
+
+class CudaFullyConnectedNet(torch.nn.Module):
+    """Drop-in for MACE's radial MLP (frozen weights): forward(x[E, h0]) -> [E, h_last]."""
+
+    def __init__(self, mlp):
+        super().__init__()
+        ok, why = mlp_supported(mlp)
+        if not ok:
+            raise ValueError(why)
+        self.hs = list(mlp.hs)
+        self.dims = self.hs
+        self.scale = float(mlp._SILU_2MOM)
+        dev = next(mlp.parameters()).device
+        self.fwd, self.bwd = [], []
+        for w in mlp.weights:
+            W = (w.detach() / np.sqrt(w.shape[0])).float().cpu().numpy()          # as the module scales it
+            self.fwd.append(_Tables([(0, W.shape[1], 1)], [(0, 0, W[None])], dev))
+            self.bwd.append(_Tables([(0, W.shape[0], 1)], [(0, 0, np.ascontiguousarray(W.T)[None])], dev))
+
+    def _launch(self, t, x, out, epilogue=None, prologue=None):
+        _lib.call('mmk_block_linear_act', _lib.ptr(x), x.shape[1], _lib.ptr(out), out.shape[1], _lib.ptr(t.blocks),
+                  t.n_blocks, _lib.ptr(t.paths), _lib.ptr(t.w), t.max_d, t.max_mul, None, None, 1, x.shape[0],
+                  int(epilogue is not None), _lib.ptr(epilogue), int(prologue is not None), _lib.ptr(prologue),
+                  self.scale, _lib.stream_of(x))
+
+    def forward(self, x):
+        return _MLPFn.apply(x, self)

@@ -63,3 +63,38 @@ def test_skip_tables_match_module():
     (gx,) = torch.autograd.grad(tp(xr, attrs), xr, g)
     gout = _apply(op.bwd, g.numpy(), elem)
     assert np.abs(gout - gx.numpy()).max() < 1e-5 * np.abs(gx.numpy()).max()
+
+
+def test_mlp_tables_match_module():
+    from mace_mps_kernels_b200.dense import CudaFullyConnectedNet
+    from mace_mps_kernels_b200.standin.modules import FullyConnectedNet
+    torch.manual_seed(2)
+    mlp = _frozen(FullyConnectedNet([8, 64, 64, 64, 320]))
+    op = CudaFullyConnectedNet(mlp)
+    x = torch.randn(11, 8)
+    c = op.scale
+    silu = lambda z: z / (1 + np.exp(-z))
+    dsilu = lambda z: (1 / (1 + np.exp(-z))) * (1 + z * (1 - 1 / (1 + np.exp(-z))))
+    h, zs = x.double().numpy(), []
+    for i, t in enumerate(op.fwd):
+        z = _apply(t, h)
+        if i < len(op.fwd) - 1:
+            zs.append(z)
+            h = c * silu(z)
+        else:
+            h = z
+    x64 = x.double().requires_grad_(True)
+    ref = copy_double(mlp)(x64)
+    assert np.abs(h - ref.detach().numpy()).max() < 1e-5 * np.abs(ref.detach().numpy()).max()
+    g = torch.randn(11, 320, dtype=torch.float64)
+    (gx,) = torch.autograd.grad(ref, x64, g)
+    gg = g.numpy()
+    for i in range(len(op.bwd) - 1, -1, -1):
+        a = gg if i == len(op.bwd) - 1 else gg * c * dsilu(zs[i])
+        gg = _apply(op.bwd[i], a)
+    assert np.abs(gg - gx.numpy()).max() < 1e-5 * np.abs(gx.numpy()).max()
+
+
+def copy_double(m):
+    import copy
+    return copy.deepcopy(m).double()

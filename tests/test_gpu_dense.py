@@ -65,6 +65,25 @@ def test_skip_tp_matches_module(cuda, N, n_elem):
     assert (gx.double().cpu() - gx64).abs().max().item() < 2e-5 * gx64.abs().max().item()
 
 
+@pytest.mark.parametrize('E,hs', [(5218, [8, 64, 64, 64, 1280]), (37, [8, 64, 64, 64, 128]), (9001, [8, 16, 2176])])
+def test_radial_mlp_matches_module(cuda, E, hs):
+    from mace_mps_kernels_b200.dense import CudaFullyConnectedNet
+    from mace_mps_kernels_b200.standin.modules import FullyConnectedNet
+    torch.manual_seed(3)
+    mlp = _frozen(FullyConnectedNet(hs)).to(cuda)
+    op = CudaFullyConnectedNet(mlp)
+    x = torch.randn(E, hs[0], device=cuda, requires_grad=True)
+    out = op(x)
+    mlp64 = copy.deepcopy(mlp).double().cpu()
+    x64 = x.detach().double().cpu().requires_grad_(True)
+    ref = mlp64(x64)
+    assert (out.double().cpu() - ref.detach()).abs().max().item() < 2e-5 * ref.abs().max().item()
+    g = torch.randn_like(out)
+    (gx,) = torch.autograd.grad(out, x, g)
+    (gx64,) = torch.autograd.grad(ref, x64, g.double().cpu())
+    assert (gx.double().cpu() - gx64).abs().max().item() < 2e-5 * gx64.abs().max().item()
+
+
 @pytest.mark.parametrize('config', ['l3_corr3', 'l3_corr3_l2hidden'])
 def test_model_all_extensions_matches_unpatched(cuda, config):
     from mace_mps_kernels_b200 import patch_model
@@ -74,6 +93,7 @@ def test_model_all_extensions_matches_unpatched(cuda, config):
     report = patch_model(met, verbose=False, edge_features=True, linears=True)
     assert not report['skipped'], report['skipped']
     assert 'interactions.0.linear_up' in report['patched'] and 'interactions.1.skip_tp' in report['patched']
+    assert 'interactions.1.conv_tp_weights' in report['patched']
     for s in (0, 1):
         st = helpers.make_structure(seed=s)
         E0, F0 = helpers.energy_forces(ref, st, cuda)
