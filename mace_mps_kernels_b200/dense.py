@@ -7,10 +7,10 @@ by 1/sqrt(fan_in)); the forward applies them all at once, the backward (gradient
 transposed paths.  With one-hot node attributes the skip connection is a linear map whose weight is selected by the
 node's element, W_e = W[:, e, :]; the kernel works on nodes grouped by element (the symmetric contraction's groups).
 
-The radial MLP of an interaction (``FullyConnectedNet``: scalar layers without biases, h <- c * silu(h @ W / sqrt(fan_in))
-except after the last layer) uses the same kernel, one launch per layer each way: the forward stores every hidden
+The hidden layers of an interaction's radial MLP (``FullyConnectedNet``: scalar layers without biases,
+h <- c * silu(h @ W / sqrt(fan_in))) use the same kernel, one launch per layer each way: the forward stores every
 pre-activation and applies c * silu in the epilogue, the backward applies c * silu'(z) to the incoming gradient as it
-loads it.
+loads it.  The last layer (no activation, NINS x C wide) stays one cuBLAS GEMM, which is faster at that size.
 
 Inference only: the weights must be frozen (``requires_grad`` False, as MACE's calculators set them), the backward is
 first order, double backward raises.  ``patch_model(model, linears=True)`` swaps every supported layer.
@@ -168,7 +168,9 @@ def mlp_supported(mod):
     return True, ''
 
 
-class _MLPFn(torch.autograd.Function):
+class _MLPHiddenFn(torch.autograd.Function):
+    """The hidden layers h_{i+1} = c * silu(h_i @ W_i) of the MLP (all but the last layer)."""
+
     @staticmethod
     def forward(ctx, x, op):
         h = x.contiguous()
@@ -176,14 +178,11 @@ class _MLPFn(torch.autograd.Function):
             raise TypeError('input must be a float32 CUDA tensor')
         N = h.shape[0]
         zs = []
-        for i, (fwd, dout) in enumerate(zip(op.fwd, op.dims[1:])):
+        for fwd, dout in zip(op.fwd, op.dims[1:]):
             out = torch.empty(N, dout, device=h.device, dtype=torch.float32)
-            if i < len(op.fwd) - 1:
-                z = torch.empty_like(out)
-                op._launch(fwd, h, out, epilogue=z)
-                zs.append(z)
-            else:
-                op._launch(fwd, h, out)
+            z = torch.empty_like(out)
+            op._launch(fwd, h, out, epilogue=z)
+            zs.append(z)
             h = out
         ctx.save_for_backward(*zs)
         ctx.op = op
@@ -195,17 +194,17 @@ class _MLPFn(torch.autograd.Function):
             raise RuntimeError(DOUBLE_BACKWARD_MSG)
         op, zs = ctx.op, ctx.saved_tensors
         g = g.contiguous()
-        L = len(op.bwd)
-        for i in range(L - 1, -1, -1):
+        for i in range(len(op.bwd) - 1, -1, -1):
             gin = torch.empty(g.shape[0], op.dims[i], device=g.device, dtype=torch.float32)
-            # the gradient reaching layer i's output passes through layer i's activation (none after the last layer)
-            op._launch(op.bwd[i], g, gin, prologue=zs[i] if i < L - 1 else None)
+            op._launch(op.bwd[i], g, gin, prologue=zs[i])            # through layer i's activation, then W_i^T
             g = gin
         return g, None
 
 
 class CudaFullyConnectedNet(torch.nn.Module):
-    """Drop-in for MACE's radial MLP (frozen weights): forward(x[E, h0]) -> [E, h_last]."""
+    """Drop-in for MACE's radial MLP (frozen weights): forward(x[E, h0]) -> [E, h_last].  The hidden layers run as the
+    block-linear kernel with the activation fused; the last layer (a plain product, large: h_last = NINS x C) is one
+    cuBLAS GEMM with the pre-scaled weight."""
 
     def __init__(self, mlp):
         super().__init__()
@@ -217,10 +216,12 @@ class CudaFullyConnectedNet(torch.nn.Module):
         self.scale = float(mlp._SILU_2MOM)
         dev = next(mlp.parameters()).device
         self.fwd, self.bwd = [], []
-        for w in mlp.weights:
+        ws = list(mlp.weights)
+        for w in ws[:-1]:
             W = (w.detach() / np.sqrt(w.shape[0])).float().cpu().numpy()          # as the module scales it
             self.fwd.append(_Tables([(0, W.shape[1], 1)], [(0, 0, W[None])], dev))
             self.bwd.append(_Tables([(0, W.shape[0], 1)], [(0, 0, np.ascontiguousarray(W.T)[None])], dev))
+        self.register_buffer('w_last', (ws[-1].detach() / np.sqrt(ws[-1].shape[0])).float().contiguous())
 
     def _launch(self, t, x, out, epilogue=None, prologue=None):
         _lib.call('mmk_block_linear_act', _lib.ptr(x), x.shape[1], _lib.ptr(out), out.shape[1], _lib.ptr(t.blocks),
@@ -229,4 +230,5 @@ class CudaFullyConnectedNet(torch.nn.Module):
                   self.scale, _lib.stream_of(x))
 
     def forward(self, x):
-        return _MLPFn.apply(x, self)
+        h = _MLPHiddenFn.apply(x, self) if self.fwd else x
+        return h @ self.w_last

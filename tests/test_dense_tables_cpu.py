@@ -76,22 +76,19 @@ def test_mlp_tables_match_module():
     silu = lambda z: z / (1 + np.exp(-z))
     dsilu = lambda z: (1 / (1 + np.exp(-z))) * (1 + z * (1 - 1 / (1 + np.exp(-z))))
     h, zs = x.double().numpy(), []
-    for i, t in enumerate(op.fwd):
+    for t in op.fwd:                                  # hidden layers (kernel), then the last layer (GEMM)
         z = _apply(t, h)
-        if i < len(op.fwd) - 1:
-            zs.append(z)
-            h = c * silu(z)
-        else:
-            h = z
+        zs.append(z)
+        h = c * silu(z)
+    h = h @ op.w_last.double().numpy()
     x64 = x.double().requires_grad_(True)
     ref = copy_double(mlp)(x64)
     assert np.abs(h - ref.detach().numpy()).max() < 1e-5 * np.abs(ref.detach().numpy()).max()
     g = torch.randn(11, 320, dtype=torch.float64)
     (gx,) = torch.autograd.grad(ref, x64, g)
-    gg = g.numpy()
+    gg = g.numpy() @ op.w_last.double().numpy().T
     for i in range(len(op.bwd) - 1, -1, -1):
-        a = gg if i == len(op.bwd) - 1 else gg * c * dsilu(zs[i])
-        gg = _apply(op.bwd[i], a)
+        gg = _apply(op.bwd[i], gg * c * dsilu(zs[i]))
     assert np.abs(gg - gx.numpy()).max() < 1e-5 * np.abs(gx.numpy()).max()
 
 
