@@ -7,7 +7,9 @@ hidden 128x0e+128x1o, l_max 3, correlation 3, 4 elements (H, C, O, Pt), r_max 5 
 slab with seeded CO/O/H adsorbates (~160 atoms, ~5 000 edges).  With N GPUs (torchrun, one process per GPU) every
 rank runs its own structure (seed = rank): weak scaling, the only collective is the per-step energy all_gather.
 
-One step = one energy + force call (model forward + autograd backward through the patched kernels).  Inputs are
+One step = one energy + force call (model forward + autograd backward through the patched kernels).  The model is
+patched with patch_model(model, edge_features=True, linears=True) on frozen weights: the reference's two ops (conv,
+symmetric contraction) plus this repository's edge-geometry, equivariant-linear and radial-MLP kernels.  Inputs are
 much smaller than L2, so L2 is flushed (256 MB write) before every timed step, outside the CUDA-event interval.
 
 The timed step is a replay of the whole E+F call captured in a CUDA graph (GraphedEnergyForces); the eager time is
@@ -69,7 +71,8 @@ def workload(rank):
 def config_dict(n_atoms, n_edges, world):
     return {'workload': f'configs[1]: MACE 128ch {HIDDEN} l_max {LMAX} corr {CORR} 4 elements r_max {RMAX}; '
                         f'Pt(100) 6x6x4 + CO/O/H, {n_atoms} atoms, {n_edges} edges per rank',
-            'model': 'ScaleShiftMACE (in-repo mace-torch 0.3.x stand-in, random weights seed 0)',
+            'model': 'ScaleShiftMACE (in-repo mace-torch 0.3.x stand-in, random weights seed 0, frozen)',
+            'patched': 'conv_tp, symmetric contraction, edge features, equivariant linears, radial MLP',
             'global_batch': world, 'atoms_per_rank': n_atoms, 'edges_per_rank': n_edges,
             'parallelism': f'dp{world} (structure batch, one structure per rank)',
             'l2': 'flushed (256 MB write) before every timed step'}
