@@ -234,23 +234,14 @@ MMK_API int mmk_block_linear(const float *x, int64_t ldx, float *out, int64_t ld
                              const int32_t *paths, const float *weights, int max_d, int max_mul_out,
                              const int32_t *perm, const int32_t *erow, int n_elem, int64_t n_nodes, void *stream);
 
-/* mmk_block_linear with the activation of an MLP layer (MACE's radial MLP: SiLU times a constant) and an optional
- * split of the input channels over several CTAs per output tile (small graphs):
+/* mmk_block_linear with the activation of an MLP layer (MACE's radial MLP: SiLU times a constant):
  *   epilogue != 0: zout = the product (pre-activation), out = act_scale * silu(zout)           (forward of a layer)
  *   prologue != 0: every input element x is multiplied by act_scale * silu'(zin) first          (input-gradient pass)
- * zout / zin have the layout of out / x.  Not both.  k_chunks = the largest number of 32-channel input chunks of any
- * output block (sum over its paths); with scratch (device floats) and counters (device int32, all zero, left zero)
- * of the sizes mmk_block_linear_workspace returns, the chunks may be split; the partial sums are added in a fixed
- * order (deterministic).  scratch = counters = NULL: no split. */
+ * zout / zin have the layout of out / x.  Not both. */
 MMK_API int mmk_block_linear_act(const float *x, int64_t ldx, float *out, int64_t ldo, const int32_t *blocks,
                                  int n_blocks, const int32_t *paths, const float *weights, int max_d, int max_mul_out,
                                  const int32_t *perm, const int32_t *erow, int n_elem, int64_t n_nodes, int epilogue,
-                                 float *zout, int prologue, const float *zin, float act_scale, int k_chunks,
-                                 float *scratch, int32_t *counters, void *stream);
-/* scratch floats and counters a call of mmk_block_linear_act with these sizes needs (0 and 0: it will not split). */
-MMK_API int mmk_block_linear_workspace(int n_blocks, int max_d, int max_mul_out, int n_elem, int64_t n_nodes,
-                                       int element_indexed, int prologue, int k_chunks, int64_t *scratch_floats,
-                                       int64_t *counters);
+                                 float *zout, int prologue, const float *zin, float act_scale, void *stream);
 
 #ifdef __cplusplus
 }

@@ -62,9 +62,7 @@ SIGNATURES = {
     'mmk_radial_bwd': (_i, [ctypes.POINTER(RadialDesc), _p, _p, _i64, _p, _p]),
     'mmk_block_linear': (_i, [_p, _i64, _p, _i64, _p, _i, _p, _p, _i, _i, _p, _p, _i, _i64, _p]),
     'mmk_block_linear_act': (_i, [_p, _i64, _p, _i64, _p, _i, _p, _p, _i, _i, _p, _p, _i, _i64, _i, _p, _i, _p,
-                                  ctypes.c_float, _i, _p, _p, _p]),
-    'mmk_block_linear_workspace': (_i, [_i, _i, _i, _i, _i64, _i, _i, _i, ctypes.POINTER(ctypes.c_int64),
-                                        ctypes.POINTER(ctypes.c_int64)]),
+                                  ctypes.c_float, _p]),
     'mmk_sc_source': (_i, [ctypes.POINTER(SCDesc), ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     'mmk_sc_layer_status': (_i, [_p, _ip, _i]),
     'mmk_elem_index': (_i, [_p, _i64, _i, _p, _p]),

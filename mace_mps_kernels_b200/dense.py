@@ -68,26 +68,12 @@ class _Tables:
         self.n_blocks = len(blocks)
         self.max_d = max(d for _, _, d in out_blocks)
         self.max_mul = max(mul for _, mul, _ in out_blocks)
-        self.k_chunks = max([sum((p[1] + 31) // 32 for p in paths[b[3]:b[3] + b[4]]) for b in blocks] + [0])
-        self._counters = None                          # split-K tile counters (zero between launches)
         self.blocks = torch.tensor(np.asarray(blocks, np.int32).reshape(-1, 5), device=device)
         self.paths = torch.tensor(np.asarray(paths, np.int32).reshape(-1, 3), device=device)
         wv = np.concatenate(w) if w else np.zeros(1, np.float32)
         self.w = torch.tensor(wv.astype(np.float32), device=device)
         if w_off >= 2 ** 31:
             raise ValueError('layer too large')
-
-    def workspace(self, x, n_elem, element_indexed, prologue):
-        """(scratch, counters) for a launch on x (None, None when the launch does not split the input channels)."""
-        import ctypes
-        sf, nc = ctypes.c_int64(0), ctypes.c_int64(0)
-        _lib.call('mmk_block_linear_workspace', self.n_blocks, self.max_d, self.max_mul, n_elem, x.shape[0],
-                  int(element_indexed), int(prologue), self.k_chunks, ctypes.byref(sf), ctypes.byref(nc))
-        if nc.value == 0:
-            return None, None
-        if self._counters is None or self._counters.numel() < nc.value or self._counters.device != x.device:
-            self._counters = torch.zeros(max(nc.value, 1024), dtype=torch.int32, device=x.device)
-        return torch.empty(sf.value, dtype=torch.float32, device=x.device), self._counters
 
 
 class _BlockLinearFn(torch.autograd.Function):
@@ -124,10 +110,9 @@ class _BlockLinearBase(torch.nn.Module):
 
     def _launch(self, t, x, ldx, out, ldo, groups):
         perm, erow, n_elem = groups if groups is not None else (None, None, 1)
-        scratch, counters = t.workspace(x, n_elem, groups is not None, False)
-        _lib.call('mmk_block_linear_act', _lib.ptr(x), ldx, _lib.ptr(out), ldo, _lib.ptr(t.blocks), t.n_blocks,
+        _lib.call('mmk_block_linear', _lib.ptr(x), ldx, _lib.ptr(out), ldo, _lib.ptr(t.blocks), t.n_blocks,
                   _lib.ptr(t.paths), _lib.ptr(t.w), t.max_d, t.max_mul, _lib.ptr(perm), _lib.ptr(erow), n_elem,
-                  x.shape[0], 0, None, 0, None, 1.0, t.k_chunks, _lib.ptr(scratch), _lib.ptr(counters),
+                  x.shape[0],
                   _lib.stream_of(x))
 
 
@@ -239,11 +224,10 @@ class CudaFullyConnectedNet(torch.nn.Module):
         self.register_buffer('w_last', (ws[-1].detach() / np.sqrt(ws[-1].shape[0])).float().contiguous())
 
     def _launch(self, t, x, out, epilogue=None, prologue=None):
-        scratch, counters = t.workspace(x, 1, False, prologue is not None)
         _lib.call('mmk_block_linear_act', _lib.ptr(x), x.shape[1], _lib.ptr(out), out.shape[1], _lib.ptr(t.blocks),
                   t.n_blocks, _lib.ptr(t.paths), _lib.ptr(t.w), t.max_d, t.max_mul, None, None, 1, x.shape[0],
                   int(epilogue is not None), _lib.ptr(epilogue), int(prologue is not None), _lib.ptr(prologue),
-                  self.scale, t.k_chunks, _lib.ptr(scratch), _lib.ptr(counters), _lib.stream_of(x))
+                  self.scale, _lib.stream_of(x))
 
     def forward(self, x):
         h = _MLPHiddenFn.apply(x, self) if self.fwd else x
