@@ -2,24 +2,27 @@
 //
 // Compiled at layer-creation time by NVRTC together with a generated header "mmk_layer.h" that bakes in one
 // TensorProduct: the sizes (MUL, XR, YD, ORR, NINS), the row accessors, and the straight-line per-edge bodies
-// fwd_edge / bwd_edge whose constants are the probed path coefficients (reference src/mace_mps_kernels/conv.py:57-88
-// measures the same numbers).
+// fwd_edge<H> / bwd_edge<H> of every instruction part H, whose constants are the probed path coefficients (reference
+// src/mace_mps_kernels/conv.py:57-88 measures the same numbers).
 //
 // Both kernels are persistent and warp-specialised:
 //   * one producer warp streams, edge by edge in CSR order, the rows an edge needs into a STAGES-deep ring of shared
 //     memory with TMA bulk copies (cp.async.bulk, completion counted on a per-stage mbarrier): W[e] (NINS*MUL floats)
 //     plus x[sender] (forward) or grad_out[receiver] (backward), plus Y[e] when its row is 16-byte sized;
-//   * CG consumer groups of MUL threads (one per channel u) take the edges round-robin: each waits for its edge's
-//     stage, runs the generated per-edge body on its channel's values and releases the stage to the producer; the
-//     groups' partial sums of a node are added in shared memory in group order.
-// Each CTA owns a contiguous range of nodes (a compact domain when atoms are ordered along a space-filling curve), so
-// consecutive nodes gather mostly the same neighbour rows (L2 hits) and the CTA's edges form one stretch of the CSR.
+//   * CG consumer groups take the edges round-robin (ring position it -> group it % CG).  A group is NP parts x
+//     MUL/CPT threads: thread (part h, u0) handles channels u0 + q*MUL/CPT (CPT channels per thread) and the
+//     instructions of part h (NP threads per channel); every part of a group reads each stage the group owns, then
+//     releases it to the producer (after a proxy fence: the next TMA copy into the stage is an async-proxy write).
+//     Partial sums of a node over groups and parts are added in shared memory in a fixed order.
+// Nodes are cut into chunks dealt round-robin to the CTAs (one contiguous range per CTA, or chunks of a few nodes on
+// large graphs so that all CTAs work in one compact window and gathered rows stay in L2); with atoms ordered along a
+// space-filling curve a chunk is a compact domain and one stretch of the CSR.
 //   forward   node = receiver; out[n] accumulated in registers over the receiver CSR segment, written once:
 //             deterministic, no atomics.
 //   backward  node = sender; x[s] in registers; per edge gW[e, :, u] (coalesced over u) and gY[e, :] (channel sum:
-//             register transpose-reduce in each warp, then across the consumer warps through shared memory, handed
-//             over with an mbarrier); gx[s] accumulated in registers, written once.  Fuses the reference's
-//             conv_bwd_x and conv_bwd_wy (conv.py:144-222), which gather x and grad_out twice.
+//             register transpose-reduce in each warp, then the last warp of the group adds the warps' partials in warp
+//             order); gx[s] accumulated in registers, written once.  Fuses the reference's conv_bwd_x and conv_bwd_wy
+//             (conv.py:144-222), which gather x and grad_out twice.
 // Every wait is bounded (about a second of clock64); on expiry the CTA records an error code in mmk_status, the
 // producer waits (bounded) for the copies it issued, and the CTA returns -- no trap, no hang.
 #include "mmk_layer.h"
