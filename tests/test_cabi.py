@@ -79,3 +79,42 @@ def test_patch_model_host_checks():
     assert not ok and 'multiple of 32' in why
     assert conv_supported(m.interactions[1].conv_tp) == (True, '')
     assert conv_supported(object())[0] is False
+
+
+def test_extension_entry_points_validate_arguments():
+    """The edge-geometry and block-linear entry points reject bad arguments before any launch (no GPU needed)."""
+    from mace_mps_kernels_b200 import _lib
+    L = _lib.lib()
+    dummy = ctypes.c_void_p(16)                      # never dereferenced: every call below fails validation first
+    assert L.mmk_sh_fwd(dummy, 10, 4, dummy, None) == _lib.MMK_ERR_UNSUPPORTED            # l_max > 3
+    assert L.mmk_sh_fwd(dummy, 0, 3, dummy, None) == _lib.MMK_OK                         # no edges: nothing to do
+    assert L.mmk_sh_bwd(None, None, 5, 2, None, None) == _lib.MMK_ERR_INVALID              # null tensors
+    w = (ctypes.c_float * 8)(*range(8))
+    d = _lib.RadialDesc(0, w, 1.0, 5.0, 5.0)
+    assert L.mmk_radial_fwd(ctypes.byref(d), dummy, 10, dummy, None) == _lib.MMK_ERR_UNSUPPORTED   # no Bessel fns
+    d = _lib.RadialDesc(8, w, 1.0, -1.0, 5.0)
+    assert L.mmk_radial_bwd(ctypes.byref(d), dummy, dummy, 10, dummy, None) == _lib.MMK_ERR_INVALID  # r_max <= 0
+    args = [dummy, 4, dummy, 4, dummy, 1, dummy, dummy, 1, 4]
+    # perm without erow
+    assert L.mmk_block_linear(*args, dummy, None, 1, 10, None) == _lib.MMK_ERR_INVALID
+    # element-indexed flag missing but several elements
+    assert L.mmk_block_linear(*args, None, None, 3, 10, None) == _lib.MMK_ERR_INVALID
+    # activation epilogue without a pre-activation buffer
+    assert L.mmk_block_linear_act(*args, None, None, 1, 10, 1, None, 0, None, ctypes.c_float(1.0),
+                                  None) == _lib.MMK_ERR_INVALID
+    assert 'zout' in L.mmk_last_error().decode()
+    # block dimension beyond the kernel's row tile
+    args[8] = 65
+    assert L.mmk_block_linear(*args, None, None, 1, 10, None) == _lib.MMK_ERR_INVALID
+
+
+def test_generated_sources_are_deterministic():
+    """Same descriptor -> byte-identical generated source (the module cache and the NVRTC cubins depend on it)."""
+    from mace_mps_kernels_b200 import conv, symmetric
+    spec = conv.ConvSpec(helpers.conv_tp('32x0e+32x1o', 3))
+    assert conv.source(spec) == conv.source(conv.ConvSpec(helpers.conv_tp('32x0e+32x1o', 3)))
+    m = helpers.make_model('32x0e+32x1o', 3, 3)
+    sc = m.products[1].symmetric_contractions
+    assert symmetric.source(symmetric.SCSpec(sc)) == symmetric.source(symmetric.SCSpec(sc))
+    assert 'sc_fwd_body' in symmetric.source(symmetric.SCSpec(sc))
+    assert 'fwd_edge' in conv.source(spec) and 'bwd_edge' in conv.source(spec)
