@@ -243,6 +243,18 @@ MMK_API int mmk_block_linear_act(const float *x, int64_t ldx, float *out, int64_
                                  const int32_t *perm, const int32_t *erow, int n_elem, int64_t n_nodes, int epilogue,
                                  float *zout, int prologue, const float *zin, float act_scale, void *stream);
 
+/* The hidden layers of MACE's radial MLP (e3nn FullyConnectedNet without biases, SiLU), all in one launch:
+ *   h_0 = x [n_rows, widths[0]],  z_l = h_{l-1} @ W_l,  h_l = act_scale * silu(z_l),  l = 1 .. n_layers.
+ * widths: host int32 [n_layers + 1], each 1..64; 1 <= n_layers <= 4.  weights: device, W_1 .. W_L packed one after
+ * the other, W_l [widths[l-1]][widths[l]] row-major, already scaled by 1/sqrt(fan_in).  Writes h_out = h_L
+ * [n_rows, widths[L]] and z_out = z_1 .. z_L packed ([n_rows, widths[l]] each, one after the other). */
+MMK_API int mmk_mlp_fwd(const float *x, int64_t n_rows, int n_layers, const int32_t *widths, const float *weights,
+                        float act_scale, float *h_out, float *z_out, void *stream);
+/* grad_x [n_rows, widths[0]] = d(sum h_L * grad_h)/dx through the same layers, from the z_out of the forward.
+ * weights_t: the transposed matrices, W_l^T [widths[l]][widths[l-1]] row-major, packed in the same order. */
+MMK_API int mmk_mlp_bwd(const float *grad_h, int64_t n_rows, int n_layers, const int32_t *widths,
+                        const float *weights_t, const float *z, float act_scale, float *grad_x, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

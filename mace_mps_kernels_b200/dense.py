@@ -8,14 +8,18 @@ transposed paths.  With one-hot node attributes the skip connection is a linear 
 node's element, W_e = W[:, e, :]; the kernel works on nodes grouped by element (the symmetric contraction's groups).
 
 The hidden layers of an interaction's radial MLP (``FullyConnectedNet``: scalar layers without biases,
-h <- c * silu(h @ W / sqrt(fan_in))) use the same kernel, one launch per layer each way: the forward stores every
-pre-activation and applies c * silu in the epilogue, the backward applies c * silu'(z) to the incoming gradient as it
-loads it.  The last layer (no activation, NINS x C wide) stays one cuBLAS GEMM, which is faster at that size.
+h <- c * silu(h @ W / sqrt(fan_in))) run in one launch each way (C ABI ``mmk_mlp_fwd`` / ``mmk_mlp_bwd``): a CTA keeps
+every layer's weights and the activations of a block of edges in shared memory; the forward stores every
+pre-activation, the backward applies c * silu'(z) to the gradient layer by layer.  Wider or deeper MLPs use the
+block-linear kernel, one launch per layer with the activation fused.  The last layer (no activation, NINS x C wide)
+stays one cuBLAS GEMM, which is faster at that size.
 
 Inference only: the weights must be frozen (``requires_grad`` False, as MACE's calculators set them), the backward is
 first order, double backward raises.  ``patch_model(model, linears=True)`` swaps every supported layer.
 """
 from __future__ import annotations
+
+import ctypes
 
 import numpy as np
 import torch
@@ -201,10 +205,45 @@ class _MLPHiddenFn(torch.autograd.Function):
         return g, None
 
 
+MLP_FUSED_MAX_WIDTH, MLP_FUSED_MAX_LAYERS = 64, 4      # limits of mmk_mlp_fwd / mmk_mlp_bwd
+
+
+class _MLPFusedFn(torch.autograd.Function):
+    """All hidden layers in one launch each way (mmk_mlp_fwd / mmk_mlp_bwd); the pre-activations are saved."""
+
+    @staticmethod
+    def forward(ctx, x, op):
+        x = x.contiguous()
+        if x.dtype != torch.float32 or not x.is_cuda:
+            raise TypeError('input must be a float32 CUDA tensor')
+        E, L = x.shape[0], len(op.hidden_widths) - 1
+        h = torch.empty(E, op.hidden_widths[-1], device=x.device, dtype=torch.float32)
+        z = torch.empty(E * sum(op.hidden_widths[1:]), device=x.device, dtype=torch.float32)
+        _lib.call('mmk_mlp_fwd', _lib.ptr(x), E, L, op.widths_c(), _lib.ptr(op.w_hidden), op.scale, _lib.ptr(h),
+                  _lib.ptr(z), _lib.stream_of(x))
+        ctx.save_for_backward(z)
+        ctx.op = op
+        return h
+
+    @staticmethod
+    def backward(ctx, g):
+        if torch.is_grad_enabled():
+            raise RuntimeError(DOUBLE_BACKWARD_MSG)
+        op, (z,) = ctx.op, ctx.saved_tensors
+        g = g.contiguous()
+        E, L = g.shape[0], len(op.hidden_widths) - 1
+        gx = torch.empty(E, op.hidden_widths[0], device=g.device, dtype=torch.float32)
+        _lib.call('mmk_mlp_bwd', _lib.ptr(g), E, L, op.widths_c(), _lib.ptr(op.w_hidden_t), _lib.ptr(z), op.scale,
+                  _lib.ptr(gx), _lib.stream_of(g))
+        return gx, None
+
+
 class CudaFullyConnectedNet(torch.nn.Module):
-    """Drop-in for MACE's radial MLP (frozen weights): forward(x[E, h0]) -> [E, h_last].  The hidden layers run as the
-    block-linear kernel with the activation fused; the last layer (a plain product, large: h_last = NINS x C) is one
-    cuBLAS GEMM with the pre-scaled weight."""
+    """Drop-in for MACE's radial MLP (frozen weights): forward(x[E, h0]) -> [E, h_last].  The hidden layers run in one
+    launch each way (``mmk_mlp_fwd`` / ``mmk_mlp_bwd``: every layer's weights and the activation tile of a block of
+    edges stay in shared memory) when they have at most 4 layers of width <= 64 (MACE: 8 -> 64 -> 64 -> 64), else as
+    one block-linear launch per layer with the activation fused.  The last layer (a plain product, large: h_last =
+    NINS x C) is one cuBLAS GEMM with the pre-scaled weight."""
 
     def __init__(self, mlp):
         super().__init__()
@@ -217,11 +256,20 @@ class CudaFullyConnectedNet(torch.nn.Module):
         dev = next(mlp.parameters()).device
         self.fwd, self.bwd = [], []
         ws = list(mlp.weights)
-        for w in ws[:-1]:
-            W = (w.detach() / np.sqrt(w.shape[0])).float().cpu().numpy()          # as the module scales it
+        scaled = [(w.detach() / np.sqrt(w.shape[0])).float() for w in ws]    # as the module scales them
+        for W in (w.cpu().numpy() for w in scaled[:-1]):
             self.fwd.append(_Tables([(0, W.shape[1], 1)], [(0, 0, W[None])], dev))
             self.bwd.append(_Tables([(0, W.shape[0], 1)], [(0, 0, np.ascontiguousarray(W.T)[None])], dev))
-        self.register_buffer('w_last', (ws[-1].detach() / np.sqrt(ws[-1].shape[0])).float().contiguous())
+        self.hidden_widths = tuple(int(h) for h in self.hs[:-1])
+        self.fused = (1 <= len(self.hidden_widths) - 1 <= MLP_FUSED_MAX_LAYERS and
+                      max(self.hidden_widths) <= MLP_FUSED_MAX_WIDTH)
+        hidden = scaled[:-1] or [torch.zeros(1, 1)]
+        self.register_buffer('w_hidden', torch.cat([w.reshape(-1) for w in hidden]).contiguous().to(dev))
+        self.register_buffer('w_hidden_t', torch.cat([w.t().reshape(-1) for w in hidden]).contiguous().to(dev))
+        self.register_buffer('w_last', scaled[-1].contiguous())
+
+    def widths_c(self):
+        return (ctypes.c_int * len(self.hidden_widths))(*self.hidden_widths)
 
     def _launch(self, t, x, out, epilogue=None, prologue=None):
         _lib.call('mmk_block_linear_act', _lib.ptr(x), x.shape[1], _lib.ptr(out), out.shape[1], _lib.ptr(t.blocks),
@@ -230,5 +278,10 @@ class CudaFullyConnectedNet(torch.nn.Module):
                   self.scale, _lib.stream_of(x))
 
     def forward(self, x):
-        h = _MLPHiddenFn.apply(x, self) if self.fwd else x
+        if not self.fwd:
+            h = x
+        elif self.fused:
+            h = _MLPFusedFn.apply(x, self)
+        else:
+            h = _MLPHiddenFn.apply(x, self)
         return h @ self.w_last

@@ -95,3 +95,42 @@ def test_mlp_tables_match_module():
 def copy_double(m):
     import copy
     return copy.deepcopy(m).double()
+
+
+def test_mlp_packed_hidden_weights():
+    """The packed buffer mmk_mlp_fwd / mmk_mlp_bwd read (W_1 .. W_L row-major, one after the other), evaluated as the
+    kernels evaluate it, against the module, forward and input gradient."""
+    from mace_mps_kernels_b200.dense import CudaFullyConnectedNet
+    from mace_mps_kernels_b200.standin.modules import FullyConnectedNet
+    torch.manual_seed(5)
+    mlp = _frozen(FullyConnectedNet([5, 30, 7, 96]))
+    op = CudaFullyConnectedNet(mlp)
+    assert op.fused and op.hidden_widths == (5, 30, 7)
+    w = op.w_hidden.double().numpy()
+    widths, c = op.hidden_widths, op.scale
+    silu = lambda z: z / (1 + np.exp(-z))
+    dsilu = lambda z: (1 / (1 + np.exp(-z))) * (1 + z * (1 - 1 / (1 + np.exp(-z))))
+    x = torch.randn(13, 5, dtype=torch.float64)
+    h, zs, off, Ws = x.numpy(), [], 0, []
+    for win, wout in zip(widths[:-1], widths[1:]):
+        W = w[off:off + win * wout].reshape(win, wout)
+        off += win * wout
+        Ws.append(W)
+        z = h @ W
+        zs.append(z)
+        h = c * silu(z)
+    assert off == w.size
+    wt, off = op.w_hidden_t.double().numpy(), 0                  # mmk_mlp_bwd's operand: W_l^T, packed alike
+    for W in Ws:
+        assert np.array_equal(wt[off:off + W.size].reshape(W.shape[1], W.shape[0]), W.T)
+        off += W.size
+    out = h @ op.w_last.double().numpy()
+    x64 = x.clone().requires_grad_(True)
+    ref = copy_double(mlp)(x64)
+    assert np.abs(out - ref.detach().numpy()).max() < 1e-5 * np.abs(ref.detach().numpy()).max()
+    g = torch.randn(13, 96, dtype=torch.float64)
+    (gx,) = torch.autograd.grad(ref, x64, g)
+    gg = g.numpy() @ op.w_last.double().numpy().T
+    for W, z in zip(reversed(Ws), reversed(zs)):
+        gg = (gg * c * dsilu(z)) @ W.T
+    assert np.abs(gg - gx.numpy()).max() < 1e-5 * np.abs(gx.numpy()).max()

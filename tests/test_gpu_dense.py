@@ -43,6 +43,23 @@ def test_linear_matches_module(cuda, irr_in, irr_out, N):
     assert torch.equal(op(x.detach()), out.detach())
 
 
+@pytest.mark.parametrize('offset', [0, 1, 2])
+def test_linear_odd_rows_and_unaligned_input(cuda, offset):
+    """Rows of an odd length (23 floats) starting at any 4-byte boundary: the kernel's 16-byte copies apply only where
+    the source is 16-byte aligned, the rest go as 4-byte copies."""
+    from mace_mps_kernels_b200.dense import CudaLinear
+    from mace_mps_kernels_b200.standin import o3
+    torch.manual_seed(4)
+    lin = _frozen(o3.Linear(o3.Irreps('3x0e+5x1o+1x2e'), o3.Irreps('7x0e+2x1o+3x2e'))).to(cuda)
+    op = CudaLinear(lin)
+    N, dim = 37, lin.irreps_in.dim
+    buf = torch.randn(N * dim + offset, device=cuda)
+    x = buf[offset:].view(N, dim)                    # storage offset: base pointer 4-byte but not 16-byte aligned
+    out = op(x)
+    ref = copy.deepcopy(lin).double().cpu()(x.double().cpu())
+    assert (out.double().cpu() - ref).abs().max().item() < 2e-5 * ref.abs().max().item()
+
+
 @pytest.mark.parametrize('N,n_elem', [(168, 4), (3001, 3), (5, 89)])
 def test_skip_tp_matches_module(cuda, N, n_elem):
     from mace_mps_kernels_b200.dense import CudaSkipTP
@@ -65,13 +82,15 @@ def test_skip_tp_matches_module(cuda, N, n_elem):
     assert (gx.double().cpu() - gx64).abs().max().item() < 2e-5 * gx64.abs().max().item()
 
 
-@pytest.mark.parametrize('E,hs', [(5218, [8, 64, 64, 64, 1280]), (37, [8, 64, 64, 64, 128]), (9001, [8, 16, 2176])])
+@pytest.mark.parametrize('E,hs', [(5218, [8, 64, 64, 64, 1280]), (37, [8, 64, 64, 64, 128]), (9001, [8, 16, 2176]),
+                                  (20011, [8, 64, 64, 64, 256]), (301, [5, 30, 7, 128]), (77, [8, 96, 64, 128])])
 def test_radial_mlp_matches_module(cuda, E, hs):
     from mace_mps_kernels_b200.dense import CudaFullyConnectedNet
     from mace_mps_kernels_b200.standin.modules import FullyConnectedNet
     torch.manual_seed(3)
     mlp = _frozen(FullyConnectedNet(hs)).to(cuda)
     op = CudaFullyConnectedNet(mlp)
+    assert op.fused == (max(hs[:-1]) <= 64)          # one launch each way for MACE's 64-wide hidden layers
     x = torch.randn(E, hs[0], device=cuda, requires_grad=True)
     out = op(x)
     mlp64 = copy.deepcopy(mlp).double().cpu()
