@@ -47,3 +47,23 @@ def test_padding_edges_do_not_change_results(cuda):
     o, op = met(dict(b)), met(dict(bp))
     assert abs(float(o['energy'].detach().sum()) - float(op['energy'].detach().sum())) < 1e-5
     assert float((o['forces'] - op['forces']).abs().max()) < 1e-6
+
+
+def test_graphed_all_extensions_matches_eager(cuda):
+    """The bench's patch set (edge features, linears, fused radial MLP; frozen weights) captured in a graph replays
+    to the eager result, and replays are bit-identical."""
+    from mace_mps_kernels_b200 import patch_model
+    from mace_mps_kernels_b200.graphs import GraphedEnergyForces
+    hidden, lmax, corr, seed = helpers.CONFIGS['l3_corr3']
+    met = helpers.make_model(hidden, lmax, corr, seed).to(cuda).requires_grad_(False)
+    rep = patch_model(met, verbose=False, edge_features=True, linears=True)
+    assert not rep['skipped'], rep['skipped']
+    b0 = S.to_device(S.structure_batch([helpers.make_structure(seed=13)], helpers.ELEMENTS, 5.0, pad_to=3000), cuda)
+    g = GraphedEnergyForces(met, b0)
+    for _ in range(3):
+        E, F = g(b0)
+    E, F = E.clone(), F.clone()
+    out = met(dict(b0))
+    assert abs(float(E.sum()) - float(out['energy'].detach().sum())) < 1e-4
+    assert float((F - out['forces']).abs().max()) < 1e-5
+    assert float((g(b0)[1] - F).abs().max()) == 0.0        # replays are deterministic
