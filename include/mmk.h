@@ -218,6 +218,28 @@ MMK_API int mmk_radial_bwd(const mmk_radial_desc *desc, const float *lengths, co
                            float *grad_lengths, void *stream);
 
 /* ------------------------------------------------------------------------------------------------------------------
+ * neighbour list (no counterpart in the reference, which takes the graph MACE builds on the host): the periodic pairs
+ * within the cutoff, built on the device
+ * ---------------------------------------------------------------------------------------------------------------- */
+
+/* Every pair (i, j, S) with 0 < |positions[j] + S . cell - positions[i]| < cutoff, S an integer cell shift along the
+ * periodic axes (matscipy / ASE neighbour_list('ijS') semantics as MACE builds its graph): edge_index[0, e] = i
+ * (sender), edge_index[1, e] = j (receiver), shifts[e] = S . cell (float32), sorted by (i, j, S); rows
+ * [n_edges, capacity) are padding edges (node 0 to itself, shift (1000, 0, 0), beyond any cutoff).
+ *   positions: device float64 [n_atoms, 3]; cell (3 row vectors, 9 doubles), pbc (3), lo / hi (3 each): host.  lo / hi
+ *   give the fractional range binned along non-periodic axes (atoms outside it are still found, only slower; NULL =
+ *   [0, 1]); they are ignored on periodic axes.
+ *   edge_index: device int64 [2, capacity]; shifts: device float32 [capacity, 3]; n_edges: device int64 = the number
+ *   of pairs; above capacity the outputs are invalid and a larger capacity is needed.
+ *   workspace: device, at least mmk_nl_workspace_bytes(...) bytes (0 = invalid arguments).
+ * Nothing synchronises with the host, so the call can be captured in a CUDA graph at a fixed capacity. */
+MMK_API size_t mmk_nl_workspace_bytes(const double *cell, const int32_t *pbc, double cutoff, const double *lo,
+                                      const double *hi, int64_t n_atoms, int64_t capacity);
+MMK_API int mmk_neighbor_list(const double *positions, int64_t n_atoms, const double *cell, const int32_t *pbc,
+                              double cutoff, const double *lo, const double *hi, int64_t capacity, int64_t *edge_index,
+                              float *shifts, int64_t *n_edges, void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------------------------------------------------
  * block linear (no counterpart in the reference, which leaves MACE's equivariant linears to e3nn): every path of one
  * equivariant linear layer in one launch
  * ---------------------------------------------------------------------------------------------------------------- */

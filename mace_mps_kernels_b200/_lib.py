@@ -63,6 +63,8 @@ SIGNATURES = {
     'mmk_block_linear': (_i, [_p, _i64, _p, _i64, _p, _i, _p, _p, _i, _i, _p, _p, _i, _i64, _p]),
     'mmk_block_linear_act': (_i, [_p, _i64, _p, _i64, _p, _i, _p, _p, _i, _i, _p, _p, _i, _i64, _i, _p, _i, _p,
                                   ctypes.c_float, _p]),
+    'mmk_nl_workspace_bytes': (_sz, [_dp, _ip, _d, _dp, _dp, _i64, _i64]),
+    'mmk_neighbor_list': (_i, [_p, _i64, _dp, _ip, _d, _dp, _dp, _i64, _p, _p, _p, _p, _sz, _p]),
     'mmk_mlp_fwd': (_i, [_p, _i64, _i, _ip, _p, ctypes.c_float, _p, _p, _p]),
     'mmk_mlp_bwd': (_i, [_p, _i64, _i, _ip, _p, _p, ctypes.c_float, _p, _p]),
     'mmk_sc_source': (_i, [ctypes.POINTER(SCDesc), ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
@@ -106,7 +108,8 @@ def check(code):
 KERNELS_PER_CALL = {'mmk_conv_fwd': 1, 'mmk_conv_bwd': 1, 'mmk_sc_fwd': 1, 'mmk_sc_bwd': 1, 'mmk_csr_build': 4,
                     'mmk_csr_build_noalloc': 4, 'mmk_elem_index': 1, 'mmk_elem_groups': 3,
                     'mmk_sh_fwd': 1, 'mmk_sh_bwd': 1, 'mmk_radial_fwd': 1, 'mmk_radial_bwd': 1,
-                    'mmk_block_linear': 1, 'mmk_block_linear_act': 1, 'mmk_mlp_fwd': 1, 'mmk_mlp_bwd': 1}
+                    'mmk_block_linear': 1, 'mmk_block_linear_act': 1, 'mmk_mlp_fwd': 1, 'mmk_mlp_bwd': 1,
+                    'mmk_neighbor_list': 10}
 LAUNCHES = collections.Counter()
 
 
