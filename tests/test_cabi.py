@@ -108,6 +108,35 @@ def test_extension_entry_points_validate_arguments():
     assert L.mmk_block_linear(*args, None, None, 1, 10, None) == _lib.MMK_ERR_INVALID
 
 
+def test_mlp_and_neighbor_list_entry_points_validate_arguments():
+    """The fused-MLP and neighbour-list entry points reject bad arguments before any launch (no GPU needed), and
+    the neighbour-list workspace size follows the binning of the cell."""
+    from mace_mps_kernels_b200 import _lib
+    L = _lib.lib()
+    dummy = ctypes.c_void_p(16)
+    widths = lambda *w: (ctypes.c_int * len(w))(*w)
+    f = ctypes.c_float(1.0)
+    assert L.mmk_mlp_fwd(dummy, 10, 5, widths(8, 8, 8, 8, 8, 8), dummy, f, dummy, dummy, None) == _lib.MMK_ERR_UNSUPPORTED
+    assert L.mmk_mlp_fwd(dummy, 10, 2, widths(8, 65, 8), dummy, f, dummy, dummy, None) == _lib.MMK_ERR_UNSUPPORTED
+    assert '1..64' in L.mmk_last_error().decode()
+    assert L.mmk_mlp_bwd(dummy, 10, 0, widths(8), dummy, dummy, f, dummy, None) == _lib.MMK_ERR_UNSUPPORTED
+    assert L.mmk_mlp_bwd(None, 10, 1, widths(8, 8), dummy, dummy, f, dummy, None) == _lib.MMK_ERR_INVALID
+    assert L.mmk_mlp_fwd(dummy, 0, 1, widths(8, 8), dummy, f, dummy, dummy, None) == _lib.MMK_OK   # no rows
+    cell = (ctypes.c_double * 9)(10, 0, 0, 0, 11, 0, 0, 0, 12)
+    pbc = (ctypes.c_int * 3)(1, 1, 1)
+    n = L.mmk_nl_workspace_bytes(cell, pbc, 5.0, None, None, 100, 4000)
+    # 2 x 2 x 2 bins: per atom 24 + 12 + 4 + 4 + 4 + 4 bytes, per edge 16, bins 4 + 4 per bin (+1), 256-byte aligned
+    assert n >= 100 * 52 + 4000 * 16 + 8 * 8 and n < 100 * 52 + 4000 * 16 + 8 * 8 + 12 * 256
+    assert L.mmk_nl_workspace_bytes(cell, pbc, 0.0, None, None, 100, 4000) == 0                  # cutoff <= 0
+    flat = (ctypes.c_double * 9)(10, 0, 0, 0, 11, 0, 0, 0, 0)
+    assert L.mmk_nl_workspace_bytes(flat, pbc, 5.0, None, None, 100, 4000) == 0                  # singular cell
+    assert 'singular' in L.mmk_last_error().decode()
+    assert L.mmk_neighbor_list(dummy, 100, cell, pbc, 5.0, None, None, 4000, dummy, dummy, dummy, dummy, 16,
+                               None) == _lib.MMK_ERR_INVALID                                     # workspace too small
+    assert L.mmk_neighbor_list(dummy, 100, cell, pbc, 5.0, None, None, 4000, None, dummy, dummy, dummy, n,
+                               None) == _lib.MMK_ERR_INVALID                                     # no edge_index
+
+
 def test_generated_sources_are_deterministic():
     """Same descriptor -> byte-identical generated source (the module cache and the NVRTC cubins depend on it)."""
     from mace_mps_kernels_b200 import conv, symmetric
