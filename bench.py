@@ -470,8 +470,7 @@ def main():
         flush_l2(flush_buf)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        b = {k: (v.to(dev, non_blocking=True) if torch.is_tensor(v) else v) for k, v in pinned.items()}
-        E, F = step(b)                       # copies into the captured graph's static inputs, replays
+        E, F = step(pinned)                  # H2D copies of the pinned inputs into the graph's static inputs, replay
         forces_host.copy_(F, non_blocking=True)
         e_host = E.detach().to('cpu', non_blocking=True)
         e1.record()
