@@ -23,7 +23,7 @@ import functools
 import math
 import re
 from collections import namedtuple
-from typing import Iterable, List, Sequence, Tuple
+from typing import List, Sequence, Tuple
 
 import numpy as np
 import torch

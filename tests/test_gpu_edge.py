@@ -1,6 +1,5 @@
 """Edge-geometry kernels (spherical harmonics, radial embedding) on the GPU against the model's own modules, and the
 whole model patched with ``edge_features=True`` against the unpatched model (the reference's tolerances)."""
-import copy
 
 import numpy as np
 import pytest

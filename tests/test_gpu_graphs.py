@@ -2,7 +2,6 @@
 new (padded) neighbour list are copied into the captured inputs."""
 import numpy as np
 import pytest
-import torch
 
 import helpers
 from mace_mps_kernels_b200 import standin as S

@@ -3,7 +3,6 @@
 Tolerance: fp32 kernels vs fp64 oracle, max |gpu - oracle| <= REL * max |oracle| (+ a tiny absolute floor for
 all-zero outputs); the CSR builder is checked bit-exactly against a stable argsort.
 """
-import ctypes
 
 import numpy as np
 import pytest

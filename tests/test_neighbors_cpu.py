@@ -6,7 +6,6 @@ with atoms outside the binned range."""
 import os
 import shutil
 import subprocess
-import sys
 
 import numpy as np
 import pytest
