@@ -23,6 +23,15 @@ CUDA-event duration against the measured HBM copy bandwidth; ops_large / rooflin
 configs[4] architecture on a bulk Cu supercell far larger than L2 (symmetric contraction against a measured FP32 GEMM
 peak); cpu_baseline = the unpatched e3nn-path model on the host cores (rank 0, N = 1 only).
 
+Extra keys, the other BASELINE configurations (skipped with --no-extras):
+  batch16      configs[2]: 16 configs[0]-style structures, padded to 6 000 edges each, sharded by structure over the
+               ranks (weak in structures per rank: N ranks share the fixed 16), graphed, energy gather per step;
+  partitioned  configs[4]: one bulk Cu system (--part-cells^3 cells, 128x0e+128x1o+128x2e) partitioned by receiving
+               atom over the ranks, halo all_to_all per interaction (strong scaling; time and bytes of the halo
+               collectives reported);
+  relax89      configs[3] (N = 1 only): 89-element model on CeO2(111) + Au13, 50-call L-BFGS loop at a fixed padded
+               graph, with the energy match against the same loop on the unpatched model.
+
 Profiling entry points (ncu --profile-from-start off ...): --profile step (three graph replays of the E+F step),
 --profile ops [--large-cells K] (one launch of every large-system op).
 """
@@ -67,12 +76,14 @@ def workload(rank):
     return st, batch
 
 
-def config_dict(n_atoms, n_edges, world):
+def config_dict(atoms_total, edges_total, world):
+    """atoms_total / edges_total: summed over the ranks (each rank evaluates its own seeded structure)."""
+    per = '' if world == 1 else f' in total over {world} structures (one per rank)'
     return {'workload': f'configs[1]: MACE 128ch {HIDDEN} l_max {LMAX} corr {CORR} 4 elements r_max {RMAX}; '
-                        f'Pt(100) 6x6x4 + CO/O/H, {n_atoms} atoms, {n_edges} edges per rank',
+                        f'Pt(100) 6x6x4 + CO/O/H, {atoms_total} atoms, {edges_total} edges{per}',
             'model': 'ScaleShiftMACE (in-repo mace-torch 0.3.x stand-in, random weights seed 0, frozen)',
             'patched': 'conv_tp, symmetric contraction, edge features, equivariant linears, radial MLP',
-            'global_batch': world, 'atoms_per_rank': n_atoms, 'edges_per_rank': n_edges,
+            'global_batch': world, 'atoms_total': atoms_total, 'edges_total': edges_total,
             'parallelism': f'dp{world} (structure batch, one structure per rank)',
             'l2': 'flushed (256 MB write) before every timed step'}
 
@@ -170,6 +181,10 @@ def conv_bytes(spec, N, E):
     return fwd, bwd
 
 
+def layer_dims(spec):
+    return [spec.x_dim, spec.y_dim, spec.w_dim, spec.out_dim]
+
+
 def conv_case(mod, x, Y, W, ei, name):
     """(fwd, bwd) closures launching one conv layer's kernels through the C ABI on preallocated buffers."""
     from mace_mps_kernels_b200.conv import graph_csr
@@ -186,7 +201,7 @@ def conv_case(mod, x, Y, W, ei, name):
                             P(gW), N, E, st)
     bf, bb = conv_bytes(mod.spec, N, E)
     return dict(op=name, kind='conv', N=N, E=E, nnz=mod.spec.nnz, fwd=fwd, bwd=bwd, fwd_bytes=bf, bwd_bytes=bb,
-                keep=(mod, o, g, gx, gY, gW, rr, re_, sr, se))
+                dims=layer_dims(mod.spec), keep=(mod, o, g, gx, gY, gW, rr, re_, sr, se))
 
 
 def sc_case(mod, x, attrs, name):
@@ -213,7 +228,8 @@ def time_cases(cases, reps, flush):
     res = []
     for c in cases:
         print(f'[bench] timing {c["op"]}', file=sys.stderr, flush=True)
-        out = {k: v for k, v in c.items() if k not in ('fwd', 'bwd', 'keep')}
+        out = {k: v for k, v in c.items() if k not in ('fwd', 'bwd', 'keep', 'dims')}
+        out['_dims'] = c.get('dims')
         for tag in ('fwd', 'bwd'):
             fn = c[tag]
             ts = []
@@ -260,19 +276,22 @@ def step_cases(model, batch):
     return cases
 
 
-LARGE_CELLS = 16
+LARGE_CELLS = 10
+TRAFFIC_FILE = os.path.join(ROOT, 'profiles', 'conv_dram_traffic.json')
 
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum, forward + backward launch) of the conv layers from the
-# ncu launch lists summarised in profiles/ef_step_cfg2_launches.md (`--profile step`) and
-# profiles/conv_sc_large_cu8_launches.md (`--profile ops --large-cells 8`, 91 514 edges); re-captured whenever the
-# kernels change.
-NCU_TRAFFIC_STEP = {'conv_tp[1]': (27.5e6 + 30.9e6, 'ncu launch list of --profile step (profiles/ef_step_cfg2_launches.md)'),
-                    'conv_tp[0]': (11.2e6 + 12.6e6, 'ncu launch list of --profile step (profiles/ef_step_cfg2_launches.md)')}
-CU8_EDGES = 91514
-NCU_TRAFFIC_CU8 = {'conv_tp[1]': (904.2e6 + 2730.3e6, 'ncu launch list of --profile ops --large-cells 8 '
-                                                    '(profiles/conv_sc_large_cu8_launches.md)'),
-                   'conv_tp[0]': (208.1e6 + 380.7e6, 'ncu launch list of --profile ops --large-cells 8 '
-                                                   '(profiles/conv_sc_large_cu8_launches.md)')}
+
+def measured_traffic(kernel_pair, N, E, spec_key):
+    """DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum, forward + backward launch) of this conv layer at
+    exactly this graph size, from the committed ncu capture (None when no capture of this exact launch exists)."""
+    if not os.path.exists(TRAFFIC_FILE):
+        return None
+    rec = json.load(open(TRAFFIC_FILE))
+    for r in rec.get('launches', []):
+        if (r.get('layer_dims') == spec_key and r.get('N') == N and r.get('E') == E
+                and set(r.get('dram_bytes', {})) >= set(kernel_pair)):
+            tot = sum(r['dram_bytes'][k] for k in kernel_pair)
+            return tot, f"ncu capture: {rec.get('command', '?')}"
+    return None
 
 
 def large_cases(dev, cells=LARGE_CELLS):
@@ -354,8 +373,11 @@ def main():
                          '--profile-from-start off): three replays of the graphed E+F step, or one launch of every '
                          'large-system op')
     ap.add_argument('--partitioned', action='store_true',
-                    help='configs[5]-style run instead: one bulk Cu system (--large-cells) partitioned by receiving '
-                         'atom over the ranks (halo exchange per interaction), strong scaling')
+                    help='only the configs[4] run: one bulk Cu system (--part-cells) partitioned by receiving atom over '
+                         'the ranks (halo exchange per interaction), strong scaling')
+    ap.add_argument('--part-cells', type=int, default=PART_CELLS, help='fcc Cu supercell edge of the partitioned run')
+    ap.add_argument('--no-extras', action='store_true',
+                    help='skip the configs[2] batch, configs[3] relaxation and configs[4] partitioned measurements')
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
 
@@ -374,7 +396,7 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
 
     torch.manual_seed(0)
     model = standin.make_model(HIDDEN, LMAX, CORR, seed=0, elements=standin.ELEMENTS_PTCOH).to(dev)
@@ -383,6 +405,10 @@ def main():
     assert not rep['skipped'] and len(rep['patched']) >= 6, rep
     st, host_batch = workload(rank)
     n_atoms, n_edges = len(st), int(host_batch['edge_index'].shape[1])
+    tot = torch.tensor([n_atoms, n_edges], dtype=torch.float64, device=dev)
+    if dist is not None:                            # every rank has its own structure: the job total is the sum
+        dist.all_reduce(tot)
+    atoms_total, edges_total = int(tot[0].item()), int(tot[1].item())
     batch = standin.to_device(host_batch, dev)
     flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)   # 2x L2, between steps
     e_all = torch.zeros(world, device=dev)
@@ -404,6 +430,10 @@ def main():
             graphed()
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
+        convs = [{'layer': f'conv_tp[{k}]', 'N': n_atoms, 'E': n_edges, 'layer_dims': layer_dims(blk.conv_tp.spec)}
+                 for k, blk in enumerate(model.interactions)]
+        print(json.dumps({'profile': 'step', 'conv_launch_order': 'per replay: conv_tp[0] fwd, conv_tp[1] fwd, '
+                          'conv_tp[1] bwd, conv_tp[0] bwd', 'convs': convs}))
         return
     if a.profile == 'ops':
         cases, info = large_cases(dev, a.large_cells)
@@ -417,6 +447,9 @@ def main():
             c['bwd']()
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
+        info['launch_order'] = [f"{c['op']} {t}" for c in cases for t in ('fwd', 'bwd')]
+        info['convs'] = [{'layer': c['op'].split()[0], 'N': c['N'], 'E': c['E'], 'layer_dims': c['dims']}
+                         for c in cases if c['kind'] == 'conv']
         print(json.dumps(info))
         return
 
@@ -503,10 +536,11 @@ def main():
                      traffic_over_algorithmic=round(traffic[0] / b, 3))
         return r
 
+    pair = ('mmk_conv_fwd_kernel', 'mmk_conv_bwd_kernel')
     dom = max((o for o in ops if o['kind'] == 'conv'), key=lambda o: o['fwd_us'] + o['bwd_us'])
     roofline = conv_roof(dom, 'dominant kernel of the timed E+F step; its data fits in L2, so it is latency-bound '
                               '(cold: L2 flushed before the launch)',
-                         traffic=NCU_TRAFFIC_STEP.get(dom['op']))
+                         traffic=measured_traffic(pair, dom['N'], dom['E'], dom['_dims']))
     large, roof_large, fp32 = None, None, None
     if not a.no_large and rank == 0:
         cases, info = large_cases(dev, a.large_cells)
@@ -515,25 +549,33 @@ def main():
         large = dict(info, ops=large_ops, clocks=clk_large.summary())
         del cases
         big = max((o for o in large['ops'] if o['kind'] == 'conv'), key=lambda o: o['fwd_us'] + o['bwd_us'])
-        tr = NCU_TRAFFIC_CU8.get(big['op'].split()[0])
-        if tr is not None:                          # per-launch bytes of the Cu 8^3 capture, scaled by the edge count
-            tr = (tr[0] * big['E'] / CU8_EDGES, tr[1] + f' x {big["E"] / CU8_EDGES:.2f} (edges)')
-        roof_large = conv_roof(big, 'inputs far larger than L2 (bulk Cu, configs[4] architecture)', traffic=tr)
+        roof_large = conv_roof(big, 'inputs far larger than L2 (bulk Cu, configs[4] architecture)',
+                               traffic=measured_traffic(pair, big['N'], big['E'], big['_dims']))
         fp32 = fp32_peak(dev)
         for o in large['ops'] + ops:
             if o['kind'] == 'sc':
                 o['fp32_peak_tflops'] = round(fp32, 1)
+
+    extras = {}
+    if not a.no_extras:
+        del graphed
+        torch.cuda.empty_cache()
+        extras['batch16'] = measure_batch16(dev, rank, world, dist, local)
+        extras['partitioned'] = measure_partitioned(dev, rank, world, dist, local, a.part_cells)
+        if world == 1:                              # one structure: not sharded, measured on a single GPU
+            extras['relax89'] = measure_relax89(dev, local)
 
     if rank == 0:
         cpu = None
         if world == 1 and not a.no_cpu_baseline:
             cpu = cpu_baseline()
         res = {
-            'metric': METRIC, 'value': round(n_atoms * world / (ms * 1e-3), 1), 'unit': UNIT, 'n_gpus': world,
+            'metric': METRIC, 'value': round(atoms_total / (ms * 1e-3), 1), 'unit': UNIT, 'n_gpus': world,
             'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': round(ms, 4), 'higher_is_better': True,
             'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded structures, '
-            'random-init weights of the configs[1] architecture)', 'config': config_dict(n_atoms, n_edges, world),
-            'e2e': {'value': round(n_atoms * world / (ms_e2e * 1e-3), 1), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
+            'random-init weights of the configs[1] architecture)',
+            'config': config_dict(atoms_total, edges_total, world),
+            'e2e': {'value': round(atoms_total / (ms_e2e * 1e-3), 1), 'unit': UNIT, 'h2d_bytes_per_step': h2d,
                     'd2h_bytes_per_step': d2h, 'ms_per_step': round(ms_e2e, 4)},
             'roofline': roofline, 'cpu_baseline': cpu, 'gpu_launches': launches, 'clocks': clk.summary(),
             'eager_ms_per_step': round(eager_ms, 3),
@@ -541,34 +583,72 @@ def main():
             'roofline_large': roof_large,
             'ops_large': None if large is None else dict(large, ops=[rounded(o) for o in large['ops']]),
         }
+        res.update(extras)
         print(json.dumps(res))
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def partitioned_arm(a, rank, world, local):
-    """E+F of one bulk Cu system (configs[4] architecture, --large-cells^3 cells) partitioned over the ranks by
-    receiving atom (mace_mps_kernels_b200.distributed): every rank evaluates its owned atoms with the patched kernels
-    on its halo-extended local graph; per interaction one halo all_to_all forward and one reverse in the backward.
-    Eager steps (the collectives sit inside autograd), CUDA events, max over ranks; value = all atoms / step time."""
-    import datetime
-    from mace_mps_kernels_b200.distributed import DistributedMACE, partition_graph
-    torch.cuda.set_device(local)
-    dev = torch.device('cuda', local)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
-    elements = [29, 30, 31, 32]
+def timed_steps(step, steps, warmup, dev, dist, local):
+    """``warmup`` untimed calls, then ``steps`` calls each bracketed by CUDA events, with a barrier and a device
+    synchronisation on both sides; returns (mean ms per step, max over ranks; clock summary)."""
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = []
+    with ClockSampler(local) as clk:
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for _ in range(steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            step()
+            e1.record()
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+    return max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in evs) / steps, dev, dist), clk.summary()
+
+
+def max_over_ranks(v, dev, dist):
+    t = torch.tensor([float(v)], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(v, dev, dist):
+    t = torch.tensor([float(v)], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t)
+    return float(t.item())
+
+
+PART_CELLS = 16
+PART_ELEMENTS = [29, 30, 31, 32]
+
+
+def measure_partitioned(dev, rank, world, dist, local, cells=PART_CELLS, steps=10, warmup=3):
+    """configs[4]-style strong scaling: one bulk fcc Cu system of cells^3 conventional cells (128x0e+128x1o+128x2e,
+    l_max 3, correlation 3, r_max 5 A, every patch option, frozen weights) partitioned over the ranks by receiving
+    atom (mace_mps_kernels_b200.distributed); per interaction one halo all_to_all forward and one reverse in the
+    backward.  Eager steps (the collectives sit inside autograd), CUDA events, max over ranks; value = all atoms /
+    step time.  Also the time spent inside the halo collectives and the bytes they move."""
+    from mace_mps_kernels_b200.distributed import COMM, DistributedMACE, partition_graph
     torch.manual_seed(0)
-    model = standin.make_model('128x0e+128x1o+128x2e', 3, 3, seed=0, elements=elements).to(dev)
-    rep = patch_model(model, verbose=False)
-    assert len(rep['patched']) == 4, rep
-    st = standin.fcc_bulk('Cu', 3.61, a.large_cells, seed=0, jitter=0.1)
+    model = standin.make_model('128x0e+128x1o+128x2e', 3, 3, seed=0, elements=PART_ELEMENTS).to(dev)
+    model.requires_grad_(False)
+    rep = patch_model(model, verbose=False, edge_features=True, linears=True)
+    assert not rep['skipped'], rep
+    st = standin.fcc_bulk('Cu', 3.61, cells, seed=0, jitter=0.1)
+    t0 = time.perf_counter()
     parts = partition_graph(st, RMAX, world)
+    part_s = time.perf_counter() - t0
     part = parts[rank]
-    dm = DistributedMACE(model, part, st.positions, elements, dev)
+    dm = DistributedMACE(model, part, st.positions, PART_ELEMENTS, dev)
     e_tot = torch.zeros(1, device=dev)
 
     def step():
@@ -578,50 +658,123 @@ def partitioned_arm(a, rank, world, local):
             dist.all_reduce(e_tot)
         return F
 
-    for _ in range(a.warmup):
-        step()
+    ms, clocks = timed_steps(step, steps, warmup, dev, dist, local)
+    COMM.enabled = True                             # one more step, metered (not part of the timed steps)
+    step()
     torch.cuda.synchronize()
-    evs = []
+    COMM.enabled = False
+    comm_ms, sent, recv, n_x = COMM.summary()
+    comm_ms = max_over_ranks(comm_ms, dev, dist)
+    halo = max_over_ranks(len(part.halo), dev, dist)
+    sent = max_over_ranks(sent, dev, dist)
+    n_edges = sum(p.edge_index.shape[1] for p in parts)
+    res = {'metric': 'E+F atom-steps/s (partitioned large system)', 'value': round(len(st) / (ms * 1e-3), 1),
+           'unit': UNIT, 'n_gpus': world, 'ms_per_step': round(ms, 3), 'scaling': 'strong', 'steps': steps,
+           'warmup': warmup,
+           'config': {'workload': f'configs[4]: MACE 128x0e+128x1o+128x2e l_max 3 corr 3, fcc Cu {cells}^3 cells, '
+                                  f'{len(st)} atoms, {n_edges} edges, partitioned by receiving atom over {world} '
+                                  f'rank(s)',
+                      'owned_atoms_per_rank': len(part.owned), 'max_halo_atoms': int(halo),
+                      'patched': ', '.join(rep['patched'][:4]) + ', ... (every patch option)',
+                      'parallelism': f'domain decomposition, {world} rank(s), NCCL all_to_all_single halo exchange',
+                      'timing': 'eager E+F steps (no CUDA graph), CUDA events, max over ranks'},
+           'halo_exchange': {'collective': 'all_to_all_single (NCCL), 2 forward + 2 reverse per step',
+                             'exchanges_per_step': n_x, 'ms_per_step_max_rank': round(comm_ms, 3),
+                             'bytes_sent_per_step_max_rank': int(sent),
+                             'share_of_step': round(comm_ms / ms, 4) if world > 1 else 0.0},
+           'partition_build_s': round(part_s, 2), 'clocks': clocks}
+    del dm, model
+    torch.cuda.empty_cache()
+    return res
+
+
+def measure_batch16(dev, rank, world, dist, local, steps=20, warmup=3):
+    """16 structures of the configs[0] slab generator (Pt(100) 4x4x4 + 5 CO + 5 H, seeds 0..15) with the
+    32-channel model, each padded to 6 000 edges; rank r evaluates structures r, r+N, ... as one batched, CUDA-graphed
+    E+F call; the only collective is the energy gather.  value = all atoms / step time (max over ranks)."""
+    from mace_mps_kernels_b200.distributed import gather_energies
+    model = standin.make_model('32x0e+32x1o', 3, 3, seed=0, elements=standin.ELEMENTS_PTCOH).to(dev)
+    model.requires_grad_(False)
+    patch_model(model, verbose=False, edge_features=True, linears=True)
+    mine = list(range(rank, 16, world))
+    sts = [standin.pt100_co_h(seed=s) for s in mine]
+    batch = standin.to_device(standin.structure_batch(sts, standin.ELEMENTS_PTCOH, RMAX, pad_to=6000), dev)
+    graphed = GraphedEnergyForces(model, batch)
+
+    def step():
+        E, _ = graphed()
+        if dist is not None:
+            gather_energies(E.sum(), world)
+        return E
+
+    ms, clocks = timed_steps(step, steps, warmup, dev, dist, local)
+    atoms = sum_over_ranks(sum(len(s) for s in sts), dev, dist)
+    res = {'metric': 'E+F atom-steps/s (batch of 16 structures)', 'value': round(atoms / (ms * 1e-3), 1),
+           'unit': UNIT, 'ms_per_step': round(ms, 3), 'ms_per_structure_per_gpu': round(ms / max(1, len(mine)), 4),
+           'structures_per_rank_max': len(mine), 'steps': steps, 'warmup': warmup,
+           'config': {'workload': 'configs[2]: 16 x (Pt(100) 4x4x4 + 5 CO + 5 H, 79 atoms), padded to 6000 edges each; '
+                                  'MACE 32x0e+32x1o l_max 3 corr 3, every patch option, CUDA-graphed',
+                      'atoms_total': int(atoms), 'parallelism': f'structure batch over {world} rank(s)'},
+           'clocks': clocks}
+    del graphed, model
+    torch.cuda.empty_cache()
+    return res
+
+
+def measure_relax89(dev, local, calls=50):
+    """the 89-element model (128x0e+128x1o, r_max 6 A) on CeO2(111) + Au13, an L-BFGS loop of ``calls``
+    E+F calls at a fixed padded graph (device neighbour list, CUDA-graphed E+F, optimiser on the device), against the
+    same loop on the unpatched model (eager) for the energies."""
+    from mace_mps_kernels_b200.relax import Relaxation, ceo2_au13_workload
+    model, st, z_table, cap = ceo2_au13_workload(dev)
+    met = copy.deepcopy(model)
+    patch_model(met, verbose=False, edge_features=True, linears=True)
+    Relaxation(met, st, z_table, 6.0, dev, cap).run(3)                      # warm-up (compilation, allocations)
+    relax = Relaxation(met, st, z_table, 6.0, dev, cap)
+    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-        for _ in range(a.steps):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            step()
-            e1.record()
-            evs.append((e0, e1))
-        torch.cuda.synchronize()
-        if dist is not None:
-            dist.barrier()
-    ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / a.steps
-    t = torch.tensor([ms], device=dev)
-    halo = torch.tensor([float(len(part.halo))], device=dev)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(halo, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        energies, _ = relax.run(calls)
+        e1.record()
+        e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    ref_e, _ = Relaxation(model, st, z_table, 6.0, dev, cap, graphed=False).run(calls)
+    dE = (energies - ref_e).abs()
+    res = {'metric': 'E+F atom-steps/s (L-BFGS loop, 89-element model)', 'value': round(len(st) * calls / (ms * 1e-3), 1),
+           'unit': UNIT, 'ms_per_call': round(ms / calls, 4), 'calls': calls,
+           'energy_first_last_eV': [round(float(energies[0]), 6), round(float(energies[-1]), 6)],
+           'max_abs_dE_vs_unpatched_loop_eV': float(dE.max()),
+           'config': {'workload': f'configs[3]: MACE 128x0e+128x1o l_max 3 corr 3, 89 elements (Z 1-89), r_max 6 A; '
+                                  f'CeO2(111) 4x4 x 3 trilayers + Au13, {len(st)} atoms, padded to {cap} edges',
+                      'loop': 'L-BFGS (memory 100, maxstep 0.2 A), device neighbour list, CUDA-graphed E+F',
+                      'timing': 'CUDA events around the whole loop (includes the optimiser and neighbour list)'},
+           'clocks': clk.summary()}
+    del relax, met, model
+    torch.cuda.empty_cache()
+    return res
+
+
+def partitioned_arm(a, rank, world, local):
+    """--partitioned: only the configs[4] partitioned measurement, printed as its own line."""
+    import datetime
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
+    res = measure_partitioned(dev, rank, world, dist, local, a.part_cells, a.steps, a.warmup)
     if rank == 0:
-        n_edges = sum(p.edge_index.shape[1] for p in parts)
-        print(json.dumps({
-            'metric': 'E+F atom-steps/s (partitioned large system)', 'value': round(len(st) / (ms * 1e-3), 1),
-            'unit': UNIT, 'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': round(ms, 3),
-            'higher_is_better': True, 'scaling': 'strong', 'dtype': 'f32', 'data': 'synthetic (seeded bulk Cu)',
-            'config': {'workload': f'configs[5]-style: MACE 128x0e+128x1o+128x2e l_max 3 corr 3, fcc Cu '
-                                   f'{a.large_cells}^3 cells, {len(st)} atoms, {n_edges} edges, partitioned by '
-                                   f'receiving atom over {world} rank(s)',
-                       'owned_atoms_per_rank': len(part.owned), 'max_halo_atoms': int(halo.item()),
-                       'parallelism': f'domain decomposition, {world} rank(s), NCCL halo exchange',
-                       'timing': 'eager E+F steps (no CUDA graph), CUDA events, max over ranks'},
-            'clocks': clk.summary()}))
+        res.update(higher_is_better=True, dtype='f32', data='synthetic (seeded bulk Cu)')
+        print(json.dumps(res))
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 
 
 def rounded(o):
-    return {k: (round(v, 2) if isinstance(v, float) else v) for k, v in o.items()}
+    return {k: (round(v, 2) if isinstance(v, float) else v) for k, v in o.items() if not k.startswith('_')}
 
 
 def reference_arm(a, rank, world):

@@ -48,11 +48,11 @@ MMK_API const char *mmk_version(void);
  * conv_tp layer
  * ---------------------------------------------------------------------------------------------------------------- */
 
-/* Description of one uvu TensorProduct (what reference src/mace_mps_kernels/conv.py:133-166 ``ConvSpec`` holds).
+/* Description of one uvu TensorProduct (what reference src/mace_mps_kernels/conv.py:57-88 ``ConvSpec`` holds).
  * terms: the effective coefficient c of path (instruction k, x component a, Y component b, output component m),
  * i.e. CG x normalisation x path weight exactly as the probed TensorProduct applies it. */
 typedef struct mmk_conv_desc {
-    int mul;                 /* channels per block, a multiple of 32 (reference conv.py:122)            */
+    int mul;                 /* channels per block, a multiple of 32 (reference conv.py:43-44)          */
     int n_in1;               /* number of x blocks                                                      */
     const int *in1_l;        /* [n_in1] degree of each x block, layout order                            */
     int n_in2;               /* number of Y blocks (multiplicity 1 each)                                */
@@ -75,7 +75,7 @@ typedef struct mmk_conv_layer mmk_conv_layer;
 
 /* Generates the layer's specialised sm_100a kernels (coefficients baked in as constants), compiles them with NVRTC
  * and loads them.  Replaces ``MetalConvTP.__init__`` -> ``ConvSpec`` + ``torch.mps.compile_shader(source(spec))``
- * (reference src/mace_mps_kernels/conv.py:356-359).  Identical descriptors share one compiled module. */
+ * (reference src/mace_mps_kernels/conv.py:277-282).  Identical descriptors share one compiled module. */
 MMK_API int mmk_conv_layer_create(const mmk_conv_desc *desc, mmk_conv_layer **layer);
 MMK_API int mmk_conv_layer_destroy(mmk_conv_layer *layer);
 /* dims of a created layer: x_dim, y_dim, out_dim, w_dim (= nins*mul) */
@@ -83,7 +83,7 @@ MMK_API int mmk_conv_layer_dims(const mmk_conv_layer *layer, int *x_dim, int *y_
 /* NVRTC-compile the generated source without loading it (needs no GPU); for build checks and tests. */
 MMK_API int mmk_conv_compile_check(const mmk_conv_desc *desc);
 /* The generated layer header (sizes, launch plan and the straight-line per-edge bodies with the baked coefficients)
- * for this descriptor, as the reference's ``source(spec)`` returns its generated Metal source (conv.py:105-107).
+ * for this descriptor, as the reference's ``source(spec)`` returns its generated Metal source (conv.py:225-226).
  * Copies at most cap bytes (NUL-terminated when it fits) and sets *len to the full length; buf may be NULL. */
 MMK_API int mmk_conv_source(const mmk_conv_desc *desc, char *buf, size_t cap, size_t *len);
 /* Error status of the layer's kernels on the current device (0 = ok; nonzero = a pipeline wait gave up and the kernel
@@ -91,7 +91,7 @@ MMK_API int mmk_conv_source(const mmk_conv_desc *desc, char *buf, size_t cap, si
 MMK_API int mmk_conv_layer_status(const mmk_conv_layer *layer, int32_t *status, int reset);
 
 /* Forward: out[n] = sum over the receiver-CSR segment of n.  Deterministic (fixed edge order), no atomics.
- * Replaces reference conv.py:109-141 (``conv_fwd`` kernel) as launched by conv.py:325-326.
+ * Replaces reference conv.py:109-141 (``conv_fwd`` kernel) as launched by conv.py:245-247.
  *   recv_rowptr [N+1], recv_eids [E] : receiver CSR (mmk_csr_build on edge_index[1])
  *   senders [E] int64                : edge_index[0]                                                          */
 MMK_API int mmk_conv_fwd(const mmk_conv_layer *layer, const float *x, const float *Y, const float *W,
@@ -102,13 +102,13 @@ MMK_API int mmk_conv_fwd(const mmk_conv_layer *layer, const float *x, const floa
  *   gx[s]  = sum_{e: sender(e)=s} dTP/dx   (per sender, atomic-free),
  *   gW[e], gY[e]                           (per edge; the channel sum of gY is a warp-shuffle + shared reduction).
  * Replaces reference conv.py:144-176 (``conv_bwd_x``) and conv.py:179-222 (``conv_bwd_wy``) as launched by
- * conv.py:340-348.  Any of gx / gY / gW may be NULL to skip that output (gY and gW are computed together). */
+ * conv.py:262-269.  Any of gx / gY / gW may be NULL to skip that output (gY and gW are computed together). */
 MMK_API int mmk_conv_bwd(const mmk_conv_layer *layer, const float *x, const float *Y, const float *W, const float *grad_out,
                  const int32_t *send_rowptr, const int32_t *send_eids, const int64_t *receivers,
                  float *gx, float *gY, float *gW, int64_t n_nodes, int64_t n_edges, void *stream);
 
 /* ------------------------------------------------------------------------------------------------------------------
- * CSR of an edge index (reference src/mace_mps_kernels/conv.py:308-314 ``csr_by``)
+ * CSR of an edge index (reference src/mace_mps_kernels/conv.py:229-235 ``csr_by``)
  * ---------------------------------------------------------------------------------------------------------------- */
 
 /* Bytes of device workspace mmk_csr_build needs for (n_nodes, n_edges). */
@@ -127,7 +127,8 @@ MMK_API int mmk_csr_build(const int64_t *index, int64_t n_edges, int64_t n_nodes
  *   n_nodes <= MMK_NOALLOC_MAX_NODES and n_edges <= MMK_NOALLOC_MAX_EDGES (17 MiB per GPU); larger inputs return
  *   MMK_ERR_INVALID without launching anything.
  * The first call on a device looks up that device's copy of the array (cudaGetSymbolAddress); make it before any
- * stream capture.  All calls share the one array: calls that overlap on the GPU (different streams, or threads)
+ * stream capture.  The address is remembered together with the device's current context and looked up again when
+ * that context changes (after cudaDeviceReset, for instance); that call is then again a first call.  All calls share the one array: calls that overlap on the GPU (different streams, or threads)
  * race and must be serialised by the caller.  The array keeps the last call's contents; everything a call reads
  * from it is written first by the same call. */
 #define MMK_NOALLOC_MAX_NODES (1 << 18)
@@ -145,7 +146,7 @@ MMK_API int mmk_csr_build_noalloc(const int64_t *index, int64_t n_edges, int64_t
  *   out[b, out_off_q + c*M_q + m] = sum_t T[elem(b), c, row_t + m] * prod_{i in idx_t} x[b, c, i]
  * T is [n_elem, C, RP] fp32 on the device (caller-owned): one column of rows per (element, channel), RP = n_rows
  * rounded up to a multiple of 4 (zero padded), so every column the kernels copy with TMA starts on a 16-byte
- * boundary.  (The reference packs T[e][row][c], symmetric.py:71-74; the B200 kernels work node-major and read one
+ * boundary.  (The reference packs T[e][row][c], symmetric.py:69, 74; the B200 kernels work node-major and read one
  * channel's column at a time.) */
 typedef struct mmk_sc_desc {
     int C;                   /* channels                                                             */
@@ -169,7 +170,7 @@ MMK_API int mmk_sc_layer_destroy(mmk_sc_layer *layer);
 MMK_API int mmk_sc_layer_dims(const mmk_sc_layer *layer, int *C, int *n_ell, int *out_dim, int *n_rows);
 MMK_API int mmk_sc_compile_check(const mmk_sc_desc *desc);
 /* The generated layer header (sizes, launch plan, the Horner-scheme term code), as the reference's ``source(spec)``
- * (symmetric.py:78-80); same buffer contract as mmk_conv_source. */
+ * (symmetric.py:82-131); same buffer contract as mmk_conv_source. */
 MMK_API int mmk_sc_source(const mmk_sc_desc *desc, char *buf, size_t cap, size_t *len);
 
 MMK_API int mmk_sc_layer_status(const mmk_sc_layer *layer, int32_t *status, int reset);

@@ -1,17 +1,18 @@
 """
-mace-b200-kernels -- fused sm_100a CUDA kernels for MACE inference on NVIDIA B200 (PyTorch ``cuda``).
+B200 (sm_100a) CUDA kernels for the two operators that dominate MACE inference, behind a one-call patcher.
 
-    from mace_mps_kernels_b200 import patch_model
-    report = patch_model(model)          # model already on a CUDA device, float32; modified in place
+Usage: build a float32 MACE model on a CUDA device, then ``report = patch_model(model)``.  The model is modified in
+place and the report lists which submodules were swapped and which were left alone (with the reason).
 
-Replaces, where supported (same contract as Yike-Ye/mace-mps-kernels, reference src/mace_mps_kernels/__init__.py):
-  * each interaction block's convolution (gather -> channel-wise tensor product -> scatter-sum) via MACE's own
-    ``conv_fusion`` hook,
-  * each product block's symmetric contraction.
-Everything else stays on the original PyTorch path, except, with ``edge_features=True`` (an extension beyond the
-reference), the model's spherical harmonics and radial embedding, which then run as one CUDA kernel each way.
-Inference only: the backward pass is first order (energies, forces, stress, relaxations, MD); double backward raises
-an error.
+What gets swapped by default:
+  * ``interactions.{i}.conv_tp`` -- the per-edge tensor product and its sum over receivers, fused into one kernel
+    pair (forward over the receiver CSR, backward over the sender CSR) and switched on through MACE's ``conv_fusion``
+    flag;
+  * ``products.{i}.symmetric_contractions`` -- evaluated as an explicit per-element polynomial in the node features.
+Opt-in extras (not in the reference package): ``edge_features=True`` for the spherical harmonics and the radial basis,
+``linears=True`` for the equivariant linears, the skip connections and the radial MLP.  Only first derivatives are
+provided, which is what energies, forces, stresses, relaxations and MD need; asking autograd for a second derivative
+through these ops raises.
 """
 import inspect
 import warnings

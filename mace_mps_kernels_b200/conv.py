@@ -4,16 +4,16 @@ Drop-in for an interaction block's ``conv_tp`` under MACE's ``conv_fusion`` path
 ``src/mace_mps_kernels/conv.py``: ``forward(node_feats, edge_attrs, tp_weights, edge_index) -> [N, OUT_DIM]`` summed
 over receivers (unnormalised; MACE divides by avg_num_neighbors afterwards).
 
-* ``conv_supported`` keeps the reference's support rules (reference conv.py:110-130).
+* ``conv_supported`` keeps the reference's support rules (reference conv.py:31-51).
 * ``ConvSpec`` measures the effective coefficient of every path (CG x normalisation x path weight, as the
   TensorProduct applies it) by probing the TensorProduct with unit inputs on channel 0, keeping |c| > 1e-7 -- the
-  reference's method (conv.py:136-167); here all instructions are probed in one batch.
+  reference's method (conv.py:57-88); here all instructions are probed in one batch.
 * The kernels are generated per layer by the C library (coefficients baked in as constants, NVRTC, sm_100a):
   persistent, warp-specialised, with the per-edge rows streamed into shared memory by TMA; forward over the receiver
   CSR (deterministic, no atomics); backward in one fused pass over the sender CSR giving gx per sender and gW, gY per
   edge.
 * The receiver and sender CSRs are built on the GPU once per edge_index tensor (both interaction layers and the
-  backward reuse them); the reference re-sorts on every forward and backward (conv.py:324, 341).
+  backward reuse them); the reference re-sorts on every forward and backward (conv.py:245, 262).
 """
 from __future__ import annotations
 
@@ -160,8 +160,23 @@ class ConvSpec:
 # ----------------------------------------------------------------------------------------------------------------------
 # CSR of the graph, built on the device once per edge_index tensor
 # ----------------------------------------------------------------------------------------------------------------------
-_CSR_CACHE = []          # [(weakref(edge_index), version, n_nodes, csr)], most recent last
+_CSR_CACHE = []          # [(weakref(edge_index), key, csr)], most recent last
 _CSR_CACHE_SIZE = 4
+
+
+def _tensor_key(t: torch.Tensor, *extra):
+    """What a cached per-tensor result depends on: the storage address, shape, strides, device and autograd version
+    counter.  In-place writes through PyTorch bump the version; writes that bypass it (DLPack, C extensions,
+    ``.data``, a CUDA-graph replay) are not seen -- call ``invalidate_graph_caches()`` after those."""
+    return (t.data_ptr(), tuple(t.shape), tuple(t.stride()), str(t.device), t._version) + extra
+
+
+def invalidate_graph_caches():
+    """Forget every cached receiver/sender CSR and element grouping.  Needed only when an ``edge_index`` or
+    ``node_attrs`` tensor's contents were changed in a way PyTorch's version counter does not see."""
+    _CSR_CACHE.clear()
+    from . import symmetric
+    symmetric._ELEM_CACHE.clear()
 
 
 def source(spec):
@@ -172,7 +187,7 @@ def source(spec):
 
 def csr_build(index: torch.Tensor, n_nodes: int):
     """(rowptr int32[n+1], eids int32[E]) with eids grouped by ``index`` in increasing edge id, on index's device
-    (the reference's ``csr_by``, conv.py:308-314)."""
+    (the reference's ``csr_by``, conv.py:229-235)."""
     E = index.numel()
     rowptr = torch.empty(n_nodes + 1, dtype=torch.int32, device=index.device)
     eids = torch.empty(E, dtype=torch.int32, device=index.device)
@@ -184,15 +199,17 @@ def csr_build(index: torch.Tensor, n_nodes: int):
 
 
 def graph_csr(edge_index: torch.Tensor, n_nodes: int):
-    """Receiver and sender CSRs of a contiguous int64 [2, E] edge_index, cached per tensor object and version."""
-    for ref, ver, n, csr in reversed(_CSR_CACHE):
-        if ref() is edge_index and ver == edge_index._version and n == n_nodes:
+    """Receiver and sender CSRs of a contiguous int64 [2, E] edge_index.  Both interaction layers and the backward of
+    one evaluation see the same edge_index tensor, so the CSRs are built once and cached, keyed on the tensor object,
+    its storage address, shape, strides and version counter, and n_nodes (see ``invalidate_graph_caches``)."""
+    key = _tensor_key(edge_index, int(n_nodes))
+    for ref, k, csr in reversed(_CSR_CACHE):
+        if ref() is edge_index and k == key:
             return csr
-    E = edge_index.shape[1]
     recv = edge_index[1]
     send = edge_index[0]
     csr = csr_build(recv, n_nodes) + csr_build(send, n_nodes)
-    _CSR_CACHE.append((weakref.ref(edge_index), edge_index._version, n_nodes, csr))
+    _CSR_CACHE.append((weakref.ref(edge_index), key, csr))
     del _CSR_CACHE[:-_CSR_CACHE_SIZE]
     return csr
 

@@ -24,7 +24,9 @@
 //             order); gx[s] accumulated in registers, written once.  Fuses the reference's conv_bwd_x and conv_bwd_wy
 //             (conv.py:144-222), which gather x and grad_out twice.
 // Every wait is bounded (about a second of clock64); on expiry the CTA records an error code in mmk_status, the
-// producer waits (bounded) for the copies it issued, and the CTA returns -- no trap, no hang.
+// producer waits (bounded) for the copies it issued, and the CTA returns -- no trap, no hang.  A test build
+// (MMK_TEST_STALL, environment MMK_TEST_STALL=1 at layer creation) has a producer that issues nothing, so the
+// consumers' waits run out with no copy in flight and the status path can be checked on a GPU.
 #include "mmk_layer.h"
 
 #define X_DIM (XR * MUL)
@@ -43,7 +45,9 @@
 #else
 #define MMK_BWD_BOUNDS(T) __launch_bounds__(T)
 #endif
-#define MMK_WAIT_BUDGET (2000000000LL)      // clock64 cycles, ~1 s
+#ifndef MMK_WAIT_BUDGET
+#define MMK_WAIT_BUDGET (2000000000LL)      // clock64 cycles, ~1 s (MMK_WAIT_CYCLES at layer creation overrides it)
+#endif
 
 // Error status of this module's kernels on this device (0 = ok); read and reset by mmk_conv_layer_status().
 __device__ int mmk_status;
@@ -361,6 +365,9 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     init_barriers(full, empty, STAGES, NP * NCW, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
 
     if (tid >= CG * GTH) {                          // producer warp
+#ifdef MMK_TEST_STALL
+        return;
+#endif
         u32 it = 0;
         auto issue = [&](u32 st, long long e, long long s, u64 *bar) {
             float *stage = smem + st * STAGE_F;
@@ -506,6 +513,9 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     init_barriers(full, empty, STAGES, GW, red_full, 2, CG * NP > 1 ? (CG * NP - 1) * NCW : 1, red_free, 2, NCW);
 
     if (tid >= CG * GTH) {
+#ifdef MMK_TEST_STALL
+        return;
+#endif
         u32 it = 0;
         auto issue = [&](u32 st, long long e, long long r, u64 *bar) {
             float *stage = smem + st * STAGE_F;

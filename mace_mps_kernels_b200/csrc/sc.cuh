@@ -19,7 +19,9 @@
 // T[e, c, row_t + m] g[b, off + c*M + m]) d(x^idx_t)/dx_i.  Waits are bounded as in conv_tp.cuh.
 #include "mmk_layer.h"
 
-#define MMK_WAIT_BUDGET (2000000000LL)
+#ifndef MMK_WAIT_BUDGET
+#define MMK_WAIT_BUDGET (2000000000LL)              // clock64 cycles, ~1 s (MMK_WAIT_CYCLES overrides it)
+#endif
 #define SC_NWARP (SC_NT * SC_CC)                      // consumer warps
 #define SC_NCH ((CH + SC_CC - 1) / SC_CC)             // channel chunks
 #define SC_UNIT_NODES (SC_NT * 32)
@@ -123,6 +125,9 @@ __device__ __forceinline__ Smem smem_setup(float *base) {
 __device__ __forceinline__ void sc_produce(const float *__restrict__ T, const int *__restrict__ erow, int n_elem,
                                            long long n_units, const Smem &s) {
     if ((threadIdx.x & 31) != 0) return;
+#ifdef MMK_TEST_STALL
+    return;                                       // test build: nothing issued, the consumers' waits run out
+#endif
     u32 it = 0;
     bool ok = true;
     for (long long u = blockIdx.x; u < n_units; u += gridDim.x, ++it) {

@@ -93,29 +93,73 @@ def partition_graph(structure, r_max, world):
     return parts
 
 
+class CommMeter:
+    """Optional accounting of the halo exchanges: while ``enabled``, every exchange records CUDA events around its
+    collective (on the current stream) and adds the bytes it sends and receives; ``summary()`` synchronises and
+    returns (milliseconds inside the collectives, bytes sent, bytes received, exchanges) and resets the counters."""
+
+    def __init__(self):
+        self.enabled, self.events, self.sent, self.recv = False, [], 0, 0
+
+    def summary(self):
+        ms = 0.0
+        if self.events:
+            self.events[-1][1].synchronize()
+            ms = sum(a.elapsed_time(b) for a, b in self.events)
+        out = (ms, self.sent, self.recv, len(self.events))
+        self.events, self.sent, self.recv = [], 0, 0
+        return out
+
+
+COMM = CommMeter()
+
+
+def _all_to_all(out, inp, out_splits, in_splits, group):
+    """``all_to_all_single`` into ``out``.  NCCL moves device memory directly; a gloo group (CPU ranks, or ranks
+    without NCCL sharing a GPU) moves host memory only, so device tensors are staged through the host."""
+    ev = None
+    if COMM.enabled and inp.is_cuda:
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record()
+        COMM.sent += inp.numel() * inp.element_size()
+        COMM.recv += out.numel() * out.element_size()
+    _all_to_all_raw(out, inp, out_splits, in_splits, group)
+    if ev is not None:
+        ev[1].record()
+        COMM.events.append(ev)
+
+
+def _all_to_all_raw(out, inp, out_splits, in_splits, group):
+    import torch.distributed as dist
+    if inp.is_cuda and dist.get_backend(group) == 'gloo':
+        host = torch.empty(out.shape, dtype=out.dtype)
+        dist.all_to_all_single(host, inp.cpu(), output_split_sizes=out_splits, input_split_sizes=in_splits,
+                               group=group)
+        out.copy_(host)
+    else:
+        dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits, group=group)
+
+
 class _HaloExchange(torch.autograd.Function):
     """x_owned [n_own, F] -> x_local [n_own + n_halo, F]; backward adds the halo gradients into their owners."""
 
     @staticmethod
     def forward(ctx, x_own, send_idx, send_counts, recv_counts, group):
-        import torch.distributed as dist
         ctx.send_counts, ctx.recv_counts, ctx.group = send_counts, recv_counts, group
         ctx.save_for_backward(send_idx)
         send = x_own.index_select(0, send_idx).contiguous()
         recv = x_own.new_empty((sum(recv_counts),) + tuple(x_own.shape[1:]))
-        dist.all_to_all_single(recv, send, output_split_sizes=recv_counts, input_split_sizes=send_counts, group=group)
+        _all_to_all(recv, send, recv_counts, send_counts, group)
         return torch.cat([x_own, recv], 0)
 
     @staticmethod
     def backward(ctx, g_local):
-        import torch.distributed as dist
         (send_idx,) = ctx.saved_tensors
         n_halo = sum(ctx.recv_counts)
         n_own = g_local.shape[0] - n_halo
         g_halo = g_local[n_own:].contiguous()
         back = g_local.new_empty((sum(ctx.send_counts),) + tuple(g_local.shape[1:]))
-        dist.all_to_all_single(back, g_halo, output_split_sizes=ctx.send_counts, input_split_sizes=ctx.recv_counts,
-                               group=ctx.group)
+        _all_to_all(back, g_halo, ctx.send_counts, ctx.recv_counts, ctx.group)
         g_own = g_local[:n_own].clone()
         g_own.index_add_(0, send_idx, back)
         return g_own, None, None, None, None

@@ -13,13 +13,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from . import conv as _conv
-from . import symmetric as _sym
-
-
-def _clear_caches():
-    _conv._CSR_CACHE.clear()
-    _sym._ELEM_CACHE.clear()
+from .conv import invalidate_graph_caches as _clear_caches
 
 
 class GraphedEnergyForces:

@@ -15,7 +15,7 @@ mace-torch and e3nn are not installed in this environment, so this module restat
 Only the attributes that ``patch_model`` and the reference's ``ConvSpec`` read are part of the contract: ``instructions``
 (``i_in1, i_in2, i_out, connection_mode, has_weight``), ``irreps_in1/in2/out`` (iterables of ``(mul, ir)`` with
 ``ir.l``), ``shared_weights``, ``internal_weights``, ``weight_numel``, ``buffers()`` and ``tp(x1, x2, w)``
-(reference ``src/mace_mps_kernels/conv.py:110-166``).
+(reference ``src/mace_mps_kernels/conv.py:31-88``).
 """
 from __future__ import annotations
 

@@ -22,19 +22,21 @@ import numpy as np
 import torch
 
 from . import _lib
-from .conv import DOUBLE_BACKWARD_MSG, _LayerHandle
+from .conv import DOUBLE_BACKWARD_MSG, _LayerHandle, _tensor_key
 
 
 def _contraction_tensors(ct):
+    """float64 numpy copies of one mace Contraction's constants: (correlation, {degree: U}, {degree: weights}, has an
+    output-component axis, M = 2L+1, n_ell).  mace keeps the top-degree weights as ``weights_max`` and the lower
+    degrees in ``weights`` ordered from degree correlation-1 down to 1."""
     corr = int(ct.correlation)
-    U = {nu: getattr(ct, f'U_matrix_{nu}').detach().cpu().double().numpy() for nu in range(1, corr + 1)}
-    W = {corr: ct.weights_max.detach().cpu().double().numpy()}
-    for j, w in enumerate(ct.weights):                      # weights[0] <-> nu = corr-1, weights[1] <-> corr-2, ...
-        W[corr - 1 - j] = w.detach().cpu().double().numpy()
-    has_m = U[1].ndim == 3                                   # [M, n_ell, p] for L > 0, [n_ell, p] for L = 0
-    M = U[1].shape[0] if has_m else 1
-    n_ell = U[1].shape[-2]
-    return corr, U, W, has_m, M, n_ell
+    as64 = lambda t: t.detach().cpu().double().numpy()
+    U = {nu: as64(getattr(ct, f'U_matrix_{nu}')) for nu in range(1, corr + 1)}
+    lower = [as64(w) for w in ct.weights]
+    W = dict(zip(range(corr, 0, -1), [as64(ct.weights_max)] + lower))
+    u1 = U[1]                                                # [M, n_ell, p] for L > 0, [n_ell, p] for L = 0
+    has_m = u1.ndim == 3
+    return corr, U, W, has_m, (u1.shape[0] if has_m else 1), u1.shape[-2]
 
 
 def _sym_map(n_ell, nu):
@@ -71,35 +73,46 @@ def sc_supported(sc):
     return True, ''
 
 
+def term_table(ct, tol=1e-12):
+    """The monomials of one contraction that survive ``tol``: ([(sorted index tuple, coefficients [n_elem, M, C])],
+    M, n_ell), highest degree first and index tuples in lexicographic order within a degree (the order the
+    reference's term list and generated kernels use, so rows agree one for one)."""
+    coeffs, M, n_ell = poly_coeffs(ct)
+    table = []
+    for nu in sorted(coeffs, reverse=True):
+        tuples, T = coeffs[nu]
+        peak = np.abs(T).reshape(-1, T.shape[-1]).max(axis=0)              # largest |coefficient| per monomial
+        table += [(tuples[s], T[..., s]) for s in np.flatnonzero(peak > tol)]
+    return table, M, n_ell
+
+
 class SCSpec:
+    """Polynomial form of a mace SymmetricContraction: per output block (one per contraction) its M, its terms
+    (index tuple, first row) and its output offset; ``T`` [n_elem, rows, C] float32 holds M consecutive rows per term
+    (one per output component)."""
+
     def __init__(self, sc, tol=1e-12):
         ok, why = sc_supported(sc)
         if not ok:
             raise ValueError(why)
-        self.blocks, rows, out_off = [], [], 0
-        self.n_ell = None
-        self.max_degree = 0
-        for ct in sc.contractions:
-            coeffs, M, n_ell = poly_coeffs(ct)
-            if self.n_ell not in (None, n_ell):
-                raise ValueError('contractions disagree on the number of feature components')
-            self.n_ell = n_ell
+        tables = [term_table(ct, tol) for ct in sc.contractions]
+        if len({n for _, _, n in tables}) != 1:
+            raise ValueError('contractions disagree on the number of feature components')
+        self.n_ell = tables[0][2]
+        self.C = int(sc.contractions[0].weights_max.shape[-1])
+        self.blocks, packed, row, out_off = [], [], 0, 0
+        for table, M, _ in tables:
             terms = []
-            for nu in sorted(coeffs, reverse=True):
-                tuples, T = coeffs[nu]
-                self.max_degree = max(self.max_degree, nu)
-                for s, idx in enumerate(tuples):
-                    v = T[..., s]                                          # [e, M, c]
-                    if np.abs(v).max() <= tol:
-                        continue
-                    terms.append((idx, len(rows)))
-                    rows += [v[:, m, :] for m in range(M)]
-            self.C = T.shape[2]
+            for idx, v in table:
+                terms.append((idx, row))
+                packed.append(v)                                           # [n_elem, M, C]: rows row .. row+M-1
+                row += M
             self.blocks.append(dict(M=M, terms=terms, out_off=out_off))
             out_off += self.C * M
-        self.out_dim, self.nrows = out_off, len(rows)
-        self.T = torch.tensor(np.stack(rows, axis=1), dtype=torch.float32)   # [e, rows, c]
+        self.out_dim, self.nrows = out_off, row
+        self.T = torch.from_numpy(np.concatenate(packed, axis=1)).float()  # [n_elem, rows, C]
         self.n_terms = sum(len(b['terms']) for b in self.blocks)
+        self.max_degree = max(len(idx) for b in self.blocks for idx, _ in b['terms'])
 
     @classmethod
     def from_table(cls, C, n_ell, block_M, block_terms, T):
@@ -154,10 +167,12 @@ def source(spec):
 
 def element_groups(node_attrs: torch.Tensor):
     """(elem int32[N], erow int32[n_elem+1], perm int32[N]): the argmax element of every node (reference
-    symmetric.py:169) and the nodes grouped by element, on the device; cached per node_attrs tensor and version."""
+    symmetric.py:169) and the nodes grouped by element, on the device.  Cached like the conv's CSRs: keyed on the
+    tensor object, its storage address, shape, strides and version counter (``conv.invalidate_graph_caches``)."""
     import weakref
-    for ref, ver, g in reversed(_ELEM_CACHE):
-        if ref() is node_attrs and ver == node_attrs._version:
+    key = _tensor_key(node_attrs)
+    for ref, k, g in reversed(_ELEM_CACHE):
+        if ref() is node_attrs and k == key:
             return g
     a = node_attrs.contiguous()
     if a.dtype != torch.float32 or not a.is_cuda:
@@ -172,7 +187,7 @@ def element_groups(node_attrs: torch.Tensor):
     ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=a.device)
     _lib.call('mmk_elem_groups', _lib.ptr(elem), N, n_elem, _lib.ptr(erow), _lib.ptr(perm), _lib.ptr(ws), nb, st)
     g = (elem, erow, perm)
-    _ELEM_CACHE.append((weakref.ref(node_attrs), node_attrs._version, g))
+    _ELEM_CACHE.append((weakref.ref(node_attrs), key, g))
     del _ELEM_CACHE[:-4]
     return g
 

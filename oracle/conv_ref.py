@@ -9,7 +9,7 @@ import torch
 
 
 def blocks(irreps):
-    """[(l, mul, offset)], total dim -- conv.py:102-107."""
+    """[(l, mul, offset)], total dim -- conv.py:23-28."""
     res, off = [], 0
     for mul, ir in irreps:
         res.append((ir.l, mul, off))
@@ -18,7 +18,7 @@ def blocks(irreps):
 
 
 def probe_coefficients(tp, tol=1e-7):
-    """Per-instruction effective coefficients c_k[a, b, m] measured with unit inputs on channel 0 -- conv.py:136-166.
+    """Per-instruction effective coefficients c_k[a, b, m] measured with unit inputs on channel 0 -- conv.py:57-88.
 
     Returns (spec dict, coef list); coef[k] = dict(k, l1, l2, l3, o1, o2, o3, terms=[(a, b, m, c)])."""
     in1, x_dim = blocks(tp.irreps_in1)
@@ -51,7 +51,7 @@ def probe_coefficients(tp, tol=1e-7):
 
 
 def csr_by(index, n):
-    """Stable sort of edges by index -> (rowptr int32[n+1], eids int32[E]) -- conv.py:308-314."""
+    """Stable sort of edges by index -> (rowptr int32[n+1], eids int32[E]) -- conv.py:229-235."""
     index = np.asarray(index, np.int64)
     order = np.argsort(index, kind='stable')
     counts = np.bincount(index, minlength=n)
@@ -69,7 +69,7 @@ def _dense(c):
 
 def conv_fwd(spec, coef, x, Y, W, send, recv, n_nodes):
     """out[n, o3 + u d3 + m] = sum_{e: recv(e)=n} W[e, k mul + u] sum_{a,b} c_k[a,b,m] x[send(e), o1 + u d1 + a]
-    Y[e, o2 + b] -- the semantics of the generated conv_fwd kernel, conv.py:188-220 (per-edge messages, then a
+    Y[e, o2 + b] -- the semantics of the generated conv_fwd kernel, conv.py:109-141 (per-edge messages, then a
     scatter-sum as e3nn does)."""
     x, Y, W = (np.asarray(t, np.float64) for t in (x, Y, W))
     mul, E = spec['mul'], Y.shape[0]
@@ -85,7 +85,7 @@ def conv_fwd(spec, coef, x, Y, W, send, recv, n_nodes):
 
 
 def conv_bwd(spec, coef, x, Y, W, g, send, recv):
-    """(gx, gY, gW) of sum(out * g) -- conv.py:223-255 (conv_bwd_x) and conv.py:258-301 (conv_bwd_wy)."""
+    """(gx, gY, gW) of sum(out * g) -- conv.py:144-176 (conv_bwd_x) and conv.py:179-222 (conv_bwd_wy)."""
     x, Y, W, g = (np.asarray(t, np.float64) for t in (x, Y, W, g))
     mul, E = spec['mul'], Y.shape[0]
     gx = np.zeros_like(x)

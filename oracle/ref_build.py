@@ -1,15 +1,16 @@
 """TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): run the reference's own generated kernels on the CPU.
 
 The reference (Yike-Ye/mace-mps-kernels, Python) generates its Metal kernels as source strings
-(src/mace_mps_kernels/conv.py:304-305 ``source``, src/mace_mps_kernels/symmetric.py:82-131 ``source``).  Those kernels
+(src/mace_mps_kernels/conv.py:225-226 ``source``, src/mace_mps_kernels/symmetric.py:82-131 ``source``).  Those kernels
 use only scalar arithmetic plus, in ``conv_bwd_wy``, a ``simd_sum`` + threadgroup reduction for d/dY.  This recipe
 takes the source the reference generates for a given spec, rewrites the Metal address-space words and attributes
 into C++ (``kernel``/``device``/``constant``/``[[...]]``/``uint``), replaces the d/dY channel reduction by a store of
 each thread's partial sums (summed afterwards in channel order), and compiles it with g++ into a shared library under
 ``oracle/_ref/`` (git-ignored), with one driver per kernel that loops over the Metal grid.
 
-It needs the reference checkout (``/root/reference``), so it only runs where that exists: in this build container,
-to generate the committed golden fixtures (tests/golden/make_golden.py).  No reference source is copied into the
+It needs a reference checkout: ``$MMK_REFERENCE_SRC`` (the checkout's ``src`` directory), else a ``reference/``
+checkout next to this repository.  It only runs where one exists, to generate the committed golden fixtures
+(tests/golden/make_golden.py); the GPU tests and the bench never need it.  No reference source is copied into the
 repository.
 """
 from __future__ import annotations
@@ -23,7 +24,8 @@ import sys
 
 import numpy as np
 
-REF_SRC = os.environ.get('MMK_REFERENCE_SRC', '/root/reference/src')
+_REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_SRC = os.environ.get('MMK_REFERENCE_SRC', os.path.join(os.path.dirname(_REPO), 'reference', 'src'))
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), '_ref')
 
 

@@ -3,9 +3,9 @@
   python tests/golden/make_golden.py
 
 For each case the reference's own code produces the expected values (reference = Yike-Ye/mace-mps-kernels v0.1.0):
-  * ``ConvSpec`` (src/mace_mps_kernels/conv.py:133-166) probes a stand-in e3nn-style uvu TensorProduct -> the path
-    coefficient table; ``csr_by`` (conv.py:308-314) -> receiver / sender CSRs;
-  * the reference's generated conv kernels (conv.py:188-301), compiled as C++ by oracle/ref_build.py -> out, gx, gY, gW
+  * ``ConvSpec`` (src/mace_mps_kernels/conv.py:57-88) probes a stand-in e3nn-style uvu TensorProduct -> the path
+    coefficient table; ``csr_by`` (conv.py:229-235) -> receiver / sender CSRs;
+  * the reference's generated conv kernels (conv.py:109-222), compiled as C++ by oracle/ref_build.py -> out, gx, gY, gW
     on seeded random inputs (a node with no edges included);
   * ``SCSpec`` (src/mace_mps_kernels/symmetric.py:52-75) on a duck-typed contraction built from seeded U / W arrays
     (stored in the fixture) -> packed coefficients T and the term list; its generated kernels (symmetric.py:82-131)
