@@ -286,6 +286,10 @@ def measured_traffic(kernel_pair, N, E, spec_key):
     if not os.path.exists(TRAFFIC_FILE):
         return None
     rec = json.load(open(TRAFFIC_FILE))
+    import hashlib
+    src = os.path.join(ROOT, 'mace_mps_kernels_b200', 'csrc', 'conv_tp.cuh')
+    if hashlib.sha1(open(src, 'rb').read()).hexdigest()[:16] != rec.get('conv_tp_cuh_sha1_16'):
+        return None                                 # captured from another version of the kernels
     for r in rec.get('launches', []):
         if (r.get('layer_dims') == spec_key and r.get('N') == N and r.get('E') == E
                 and set(r.get('dram_bytes', {})) >= set(kernel_pair)):

@@ -278,6 +278,23 @@ MMK_API int mmk_mlp_fwd(const float *x, int64_t n_rows, int n_layers, const int3
 MMK_API int mmk_mlp_bwd(const float *grad_h, int64_t n_rows, int n_layers, const int32_t *widths,
                         const float *weights_t, const float *z, float act_scale, float *grad_x, void *stream);
 
+/* ------------------------------------------------------------------------------------------------------------------
+ * float32 GEMM on the tensor cores (no counterpart in the reference, which leaves MACE's radial MLP to PyTorch):
+ * the last layer of the radial MLP, W[E, NINS*C] = h[E, 64] . Wr, and its input gradient, on tcgen05 (kind::tf32)
+ * with the 3xTF32 split (a = tf32(a) + tf32(a - tf32(a)); the three cross products that matter are accumulated in
+ * float32), so the result has float32 accuracy.
+ * ---------------------------------------------------------------------------------------------------------------- */
+
+/* hi[i] = tf32(x[i]) (round to nearest), lo[i] = tf32(x[i] - hi[i]): the split of a constant operand. */
+MMK_API int mmk_tf32_split(const float *x, float *hi, float *lo, int64_t n, void *stream);
+/* C[M, N] = A[M, K] . B[N, K]^T, all float32 row-major (A row i at A + i*lda, B row j at B + j*ldb, C row i at
+ * C + i*ldc); B given split (mmk_tf32_split).  K, lda, ldb, ldc multiples of 4; A, B_hi, B_lo, C 16-byte aligned.
+ * Tiles of 128 rows x 64/128/256 columns, accumulator in tensor memory. */
+MMK_API int mmk_gemm_tf32x3(const float *A, int64_t lda, const float *B_hi, const float *B_lo, int64_t ldb, float *C,
+                            int64_t ldc, int64_t M, int64_t N, int64_t K, void *stream);
+/* Nonzero when a GEMM's pipeline wait gave up (its output is invalid).  Synchronises the device; reset clears it. */
+MMK_API int mmk_gemm_status(int32_t *status, int reset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -73,6 +73,9 @@ SIGNATURES = {
     'mmk_elem_groups': (_i, [_p, _i64, _i, _p, _p, _p, _sz, _p]),
     'mmk_sc_fwd': (_i, [_p, _p, _p, _p, _i, _p, _p, _i64, _p]),
     'mmk_sc_bwd': (_i, [_p, _p, _p, _p, _i, _p, _p, _p, _i64, _p]),
+    'mmk_tf32_split': (_i, [_p, _p, _p, _i64, _p]),
+    'mmk_gemm_tf32x3': (_i, [_p, _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _p]),
+    'mmk_gemm_status': (_i, [_ip, _i]),
 }
 
 _lib = None
@@ -109,7 +112,7 @@ KERNELS_PER_CALL = {'mmk_conv_fwd': 1, 'mmk_conv_bwd': 1, 'mmk_sc_fwd': 1, 'mmk_
                     'mmk_csr_build_noalloc': 4, 'mmk_elem_index': 1, 'mmk_elem_groups': 3,
                     'mmk_sh_fwd': 1, 'mmk_sh_bwd': 1, 'mmk_radial_fwd': 1, 'mmk_radial_bwd': 1,
                     'mmk_block_linear': 1, 'mmk_block_linear_act': 1, 'mmk_mlp_fwd': 1, 'mmk_mlp_bwd': 1,
-                    'mmk_neighbor_list': 10}
+                    'mmk_neighbor_list': 10, 'mmk_tf32_split': 1, 'mmk_gemm_tf32x3': 1}
 LAUNCHES = collections.Counter()
 
 

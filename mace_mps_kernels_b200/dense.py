@@ -12,7 +12,7 @@ h <- c * silu(h @ W / sqrt(fan_in))) run in one launch each way (C ABI ``mmk_mlp
 every layer's weights and the activations of a block of edges in shared memory; the forward stores every
 pre-activation, the backward applies c * silu'(z) to the gradient layer by layer.  Wider or deeper MLPs use the
 block-linear kernel, one launch per layer with the activation fused.  The last layer (no activation, NINS x C wide)
-stays one cuBLAS GEMM, which is faster at that size.
+is a float32 GEMM on the tensor cores (``gemm.TensorCoreLinear``: tcgen05 with the 3xTF32 split), both ways.
 
 Inference only: the weights must be frozen (``requires_grad`` False, as MACE's calculators set them), the backward is
 first order, double backward raises.  ``patch_model(model, linears=True)`` swaps every supported layer.
@@ -243,7 +243,7 @@ class CudaFullyConnectedNet(torch.nn.Module):
     launch each way (``mmk_mlp_fwd`` / ``mmk_mlp_bwd``: every layer's weights and the activation tile of a block of
     edges stay in shared memory) when they have at most 4 layers of width <= 64 (MACE: 8 -> 64 -> 64 -> 64), else as
     one block-linear launch per layer with the activation fused.  The last layer (a plain product, large: h_last =
-    NINS x C) is one cuBLAS GEMM with the pre-scaled weight."""
+    NINS x C) is one tensor-core GEMM each way with the pre-scaled weight (``gemm.TensorCoreLinear``)."""
 
     def __init__(self, mlp):
         super().__init__()
@@ -267,6 +267,8 @@ class CudaFullyConnectedNet(torch.nn.Module):
         self.register_buffer('w_hidden', torch.cat([w.reshape(-1) for w in hidden]).contiguous().to(dev))
         self.register_buffer('w_hidden_t', torch.cat([w.t().reshape(-1) for w in hidden]).contiguous().to(dev))
         self.register_buffer('w_last', scaled[-1].contiguous())
+        from .gemm import TensorCoreLinear
+        self.last = TensorCoreLinear(scaled[-1].to(dev))
 
     def widths_c(self):
         return (ctypes.c_int * len(self.hidden_widths))(*self.hidden_widths)
@@ -284,4 +286,4 @@ class CudaFullyConnectedNet(torch.nn.Module):
             h = _MLPFusedFn.apply(x, self)
         else:
             h = _MLPHiddenFn.apply(x, self)
-        return h @ self.w_last
+        return self.last(h)

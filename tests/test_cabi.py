@@ -147,3 +147,29 @@ def test_generated_sources_are_deterministic():
     assert symmetric.source(symmetric.SCSpec(sc)) == symmetric.source(symmetric.SCSpec(sc))
     assert 'sc_fwd_body' in symmetric.source(symmetric.SCSpec(sc))
     assert 'fwd_edge' in conv.source(spec) and 'bwd_edge' in conv.source(spec)
+
+
+def test_gemm_entry_points_validate_arguments():
+    """Argument errors are reported before anything is launched (no GPU needed)."""
+    from mace_mps_kernels_b200 import _lib
+    L = _lib.lib()
+    p = ctypes.c_void_p(16)                                    # never dereferenced: validation fails first
+    assert L.mmk_gemm_tf32x3(p, 64, p, p, 64, p, 64, -1, 8, 64, None) == _lib.MMK_ERR_INVALID
+    assert L.mmk_gemm_tf32x3(p, 64, p, p, 64, p, 64, 10, 8, 62, None) == _lib.MMK_ERR_INVALID     # K % 4
+    assert L.mmk_gemm_tf32x3(p, 32, p, p, 64, p, 64, 10, 8, 64, None) == _lib.MMK_ERR_INVALID     # lda < K
+    assert L.mmk_gemm_tf32x3(ctypes.c_void_p(20), 64, p, p, 64, p, 64, 10, 8, 64, None) == _lib.MMK_ERR_INVALID
+    assert L.mmk_gemm_tf32x3(None, 64, p, p, 64, p, 64, 10, 8, 64, None) == _lib.MMK_ERR_INVALID
+    assert L.mmk_gemm_tf32x3(p, 64, p, p, 64, p, 64, 0, 8, 64, None) == _lib.MMK_OK                # empty
+    assert L.mmk_tf32_split(p, p, p, -1, None) == _lib.MMK_ERR_INVALID
+
+
+def test_host_tf32_split():
+    import numpy as np
+    import torch
+    from mace_mps_kernels_b200.gemm import tf32_split_host
+    x = torch.randn(10000, dtype=torch.float32) * torch.logspace(-10, 10, 10000)
+    hi, lo = tf32_split_host(x)
+    assert (hi.numpy().view(np.uint32) & 0x1FFF == 0).all() and (lo.numpy().view(np.uint32) & 0x1FFF == 0).all()
+    r = (x.double() - hi.double() - lo.double()).abs() / x.double().abs()
+    assert float(r.max()) < 2 ** -21
+    assert float(((hi.double() - x.double()).abs() / x.double().abs()).max()) <= 2 ** -11
