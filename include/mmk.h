@@ -75,7 +75,11 @@ typedef struct mmk_conv_layer mmk_conv_layer;
 
 /* Generates the layer's specialised sm_100a kernels (coefficients baked in as constants), compiles them with NVRTC
  * and loads them.  Replaces ``MetalConvTP.__init__`` -> ``ConvSpec`` + ``torch.mps.compile_shader(source(spec))``
- * (reference src/mace_mps_kernels/conv.py:277-282).  Identical descriptors share one compiled module. */
+ * (reference src/mace_mps_kernels/conv.py:277-282).  Identical descriptors share one compiled module.  The handle also
+ * owns, on the device current at creation, the scratch of the edge-balanced work split that small graphs use (two
+ * rows per CTA for the pieces of nodes whose edges straddle CTA ranges, and one flag per CTA): forward and backward
+ * launches of one handle must therefore be ordered (one stream, or explicit events); on another device the handle
+ * falls back to node ranges. */
 MMK_API int mmk_conv_layer_create(const mmk_conv_desc *desc, mmk_conv_layer **layer);
 MMK_API int mmk_conv_layer_destroy(mmk_conv_layer *layer);
 /* dims of a created layer: x_dim, y_dim, out_dim, w_dim (= nins*mul) */
@@ -226,7 +230,8 @@ MMK_API int mmk_radial_bwd(const mmk_radial_desc *desc, const float *lengths, co
 /* Every pair (i, j, S) with 0 < |positions[j] + S . cell - positions[i]| < cutoff, S an integer cell shift along the
  * periodic axes (matscipy / ASE neighbour_list('ijS') semantics as MACE builds its graph): edge_index[0, e] = i
  * (sender), edge_index[1, e] = j (receiver), shifts[e] = S . cell (float32), sorted by (i, j, S); rows
- * [n_edges, capacity) are padding edges (node 0 to itself, shift (1000, 0, 0), beyond any cutoff).
+ * [n_edges, capacity) are padding edges (padding edge k: node k mod n_atoms to itself, shift (1000, 0, 0), beyond
+ * any cutoff).
  *   positions: device float64 [n_atoms, 3]; cell (3 row vectors, 9 doubles), pbc (3), lo / hi (3 each): host.  lo / hi
  *   give the fractional range binned along non-periodic axes (atoms outside it are still found, only slower; NULL =
  *   [0, 1]); they are ignored on periodic axes.
@@ -289,9 +294,14 @@ MMK_API int mmk_mlp_bwd(const float *grad_h, int64_t n_rows, int n_layers, const
 MMK_API int mmk_tf32_split(const float *x, float *hi, float *lo, int64_t n, void *stream);
 /* C[M, N] = A[M, K] . B[N, K]^T, all float32 row-major (A row i at A + i*lda, B row j at B + j*ldb, C row i at
  * C + i*ldc); B given split (mmk_tf32_split).  K, lda, ldb, ldc multiples of 4; A, B_hi, B_lo, C 16-byte aligned.
- * Tiles of 128 rows x 64/128/256 columns, accumulator in tensor memory. */
+ * Tiles of 128 rows x 64/128/256 columns, accumulator in tensor memory.  Outputs with fewer tiles than SMs split K
+ * over several CTAs when a workspace of mmk_gemm_workspace_bytes(M, N, K) bytes (16-byte aligned, zero-filled before
+ * its first use; every call leaves its counters at zero) is given; with workspace NULL (or too small) they do not.
+ * Deterministic either way.  Calls that share a workspace must be ordered on the GPU. */
+MMK_API size_t mmk_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 MMK_API int mmk_gemm_tf32x3(const float *A, int64_t lda, const float *B_hi, const float *B_lo, int64_t ldb, float *C,
-                            int64_t ldc, int64_t M, int64_t N, int64_t K, void *stream);
+                            int64_t ldc, int64_t M, int64_t N, int64_t K, void *workspace, size_t workspace_bytes,
+                            void *stream);
 /* Nonzero when a GEMM's pipeline wait gave up (its output is invalid).  Synchronises the device; reset clears it. */
 MMK_API int mmk_gemm_status(int32_t *status, int reset);
 

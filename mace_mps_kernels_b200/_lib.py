@@ -74,7 +74,8 @@ SIGNATURES = {
     'mmk_sc_fwd': (_i, [_p, _p, _p, _p, _i, _p, _p, _i64, _p]),
     'mmk_sc_bwd': (_i, [_p, _p, _p, _p, _i, _p, _p, _p, _i64, _p]),
     'mmk_tf32_split': (_i, [_p, _p, _p, _i64, _p]),
-    'mmk_gemm_tf32x3': (_i, [_p, _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _p]),
+    'mmk_gemm_workspace_bytes': (_sz, [_i64, _i64, _i64]),
+    'mmk_gemm_tf32x3': (_i, [_p, _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _p, _sz, _p]),
     'mmk_gemm_status': (_i, [_ip, _i]),
 }
 

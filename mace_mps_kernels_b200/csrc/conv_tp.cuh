@@ -149,12 +149,134 @@ __device__ __forceinline__ float warp_transpose_reduce16(float (&v)[16]) {
 // ordered along a space-filling curve, its edges one stretch of the CSR) or a few nodes (all CTAs then work inside one
 // compact window of G*nb atoms at a time, so the rows they gather stay in L2).  Every chunk is a contiguous stretch of
 // the CSR.
-__device__ __forceinline__ bool next_chunk(long long &c, long long nb, long long n_nodes, long long &n0, long long &n1) {
+// Edge-balanced split (small graphs: nb < 0): CTA c of G takes the CSR positions [q0, q1) = [E c / G, E (c+1) / G),
+// so every CTA has the same number of edges whatever the node degrees; its nodes are those with an edge in the range
+// plus the edgeless nodes whose row starts in it.  A node whose edges straddle a boundary is computed in pieces:
+// every CTA but the one holding the node's last edge writes its piece of the node's row to part[2c] and raises
+// flags[c]; the CTA holding the last edge keeps its own piece in part[2c + 1] and, after its range, waits (bounded) for
+// the flags of the earlier pieces and writes the row as the sum of the pieces in CTA order (deterministic).  A CTA
+// raises its flag before it waits, and waits only on lower CTAs, so the chain resolves; the grid is never larger than
+// the CTAs resident at once.  Node-chunk mode (nb > 0) has q0 = 0, q1 = E: no clipping, no pieces.
+struct ERange {
+    long long q0, q1, n_first, n_end;
+};
+
+__device__ __forceinline__ long long rowptr_lower_bound(const int *__restrict__ rowptr, long long n_nodes,
+                                                        long long q) {
+    long long lo = 0, hi = n_nodes;                          // rowptr[n_nodes] = E >= q
+    while (lo < hi) {
+        const long long mid = (lo + hi) >> 1;
+        if (rowptr[mid] >= q) hi = mid;
+        else lo = mid + 1;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ ERange edge_range(const int *__restrict__ rowptr, long long n_nodes, long long n_edges,
+                                             long long nb) {
+    ERange r{0, n_edges, 0, n_nodes};
+    if (nb >= 0) return r;
+    const long long c = blockIdx.x, G = gridDim.x;
+    r.q0 = n_edges * c / G;
+    r.q1 = n_edges * (c + 1) / G;
+    const long long lo = rowptr_lower_bound(rowptr, n_nodes, r.q0);
+    r.n_first = (lo > 0 && rowptr[lo] > r.q0) ? lo - 1 : lo;          // lo - 1: a node continued from CTA c - 1
+    r.n_end = c == G - 1 ? n_nodes : rowptr_lower_bound(rowptr, n_nodes, r.q1);
+    return r;
+}
+
+// CTA c' whose range holds CSR position q
+__device__ __forceinline__ long long cta_of_edge(long long q, long long n_edges) {
+    const long long G = gridDim.x;
+    long long c = q * G / (n_edges > 0 ? n_edges : 1);
+    while (c + 1 < G && n_edges * (c + 1) / G <= q) ++c;
+    while (c > 0 && n_edges * c / G > q) --c;
+    return c;
+}
+
+__device__ __forceinline__ bool next_chunk(long long &c, long long nb, long long n_nodes, const ERange &er,
+                                           long long &n0, long long &n1) {
+    if (nb < 0) {                                            // edge-balanced: one range per CTA
+        if (c != blockIdx.x) return false;
+        n0 = er.n_first;
+        n1 = er.n_end;
+        c += gridDim.x;
+        return true;
+    }
     if (c * nb >= n_nodes) return false;
     n0 = c * nb;
     n1 = min(n_nodes, n0 + nb);
     c += gridDim.x;
     return true;
+}
+
+// Where the finished row of node n goes: the output row when the CTA holds all of n's edges, else its piece's slot
+// (part[2c] when later CTAs hold more of n's edges, part[2c + 1] when this CTA holds the last ones).
+__device__ __forceinline__ float *row_of_node(float *out, float *part, long long n, int row, const int *rowptr,
+                                              const ERange &er) {
+    const bool head = rowptr[n] < er.q0, tail = rowptr[n + 1] > er.q1;
+    if (!head && !tail) return out + n * (long long)row;
+    return part + (2LL * blockIdx.x + (tail ? 0 : 1)) * row;
+}
+
+__device__ __forceinline__ int ld_acquire(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release(int *p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// End of an edge-balanced range, run by every consumer thread (ct = consumer thread index, NC = consumer threads):
+// publish this CTA's piece of its last node, then finish its first node if the CTA holds that node's last edges.
+// Every warp arrives on `done` once its stores are fenced; thread 0 waits for all of them, raises the flag, waits
+// for the flags of the earlier pieces and releases the others through `go`.  All waits are bounded.
+template <int NC>
+__device__ __forceinline__ void finish_pieces(float *out, float *part, int *flags, int row, const int *rowptr,
+                                              const ERange &er, long long n_edges, u64 *done, u64 *go, int ct,
+                                              int lane) {
+    const long long c = blockIdx.x;
+    const bool any = er.n_end > er.n_first;
+    const bool publish = any && rowptr[er.n_end] > er.q1;
+    const bool finalize = any && rowptr[er.n_first] < er.q0 && rowptr[er.n_first + 1] <= er.q1;
+    __threadfence();                                         // this thread's rows, visible GPU-wide
+    __syncwarp();
+    if (lane == 0) mbar_arrive(done);
+    long long c_first = c;
+    if (finalize) c_first = cta_of_edge(rowptr[er.n_first], n_edges);
+    __shared__ int pieces_ok;
+    if (ct == 0) {
+        bool ok = mbar_wait(done, 0);
+        if (ok && publish) st_release(&flags[c], 1);
+        if (ok && finalize) {
+            for (long long k = c_first; k < c && ok; ++k) {
+                const long long t0 = clock64();
+                while (ld_acquire(&flags[k]) == 0)
+                    if (clock64() - t0 > MMK_WAIT_BUDGET) {
+                        ok = false;
+                        break;
+                    }
+            }
+            for (long long k = c_first; k < c; ++k) flags[k] = 0;   // read once: ready for the next launch
+        }
+        if (!ok) atomicExch(&mmk_status, 10);
+        pieces_ok = ok ? 1 : 0;
+        mbar_arrive(go);
+        if (!ok) return;
+    }
+    if (!finalize) return;
+    if (!mbar_wait(go, 0)) {
+        if (lane == 0) atomicExch(&mmk_status, 11);
+        return;
+    }
+    if (!pieces_ok) return;                                  // thread 0 gave up on the flags: leave the row
+    float *dst = out + er.n_first * (long long)row;
+    for (int i = ct; i < row; i += NC) {
+        float v = 0.0f;
+        for (long long k = c_first; k < c; ++k) v += __ldcg(part + 2 * k * row + i);
+        dst[i] = v + __ldcg(part + (2 * c + 1) * row + i);
+    }
 }
 
 // Producer: stream the TMA copies of the CTA's edges [rowptr[n0], rowptr[n1]) in CSR order.  The warp fetches the
@@ -164,11 +286,11 @@ __device__ __forceinline__ bool next_chunk(long long &c, long long nb, long long
 template <int STAGES, class Issue>
 __device__ __forceinline__ bool produce(const int *__restrict__ rowptr, const int *__restrict__ eids,
                                         const long long *__restrict__ other, long long n0, long long n1,
-                                        long long n_nodes, long long n_edges, u64 *full, u64 *empty, u32 &it,
-                                        Issue issue) {
+                                        const ERange &er, long long n_nodes, long long n_edges, u64 *full, u64 *empty,
+                                        u32 &it, Issue issue) {
     const int lane = threadIdx.x & 31;
     if (n0 >= n1) return true;
-    const int q0 = rowptr[n0], q1 = rowptr[n1];
+    const int q0 = (int)max((long long)rowptr[n0], er.q0), q1 = (int)min((long long)rowptr[n1], er.q1);
     long long e_next = 0, o_next = 0;
     if (q0 + lane < q1) {
         e_next = eids[q0 + lane];
@@ -274,7 +396,8 @@ __device__ __forceinline__ void load_y(const float *ys, const float *__restrict_
 }
 
 __device__ __forceinline__ void init_barriers(u64 *full, u64 *empty, int stages, u32 ncw, u64 *extra, int n_extra,
-                                              u32 extra_count, u64 *extra2, int n_extra2, u32 extra2_count) {
+                                              u32 extra_count, u64 *extra2, int n_extra2, u32 extra2_count,
+                                              u64 *edone, u32 n_cons_warps) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(&full[s], 1);
@@ -282,6 +405,8 @@ __device__ __forceinline__ void init_barriers(u64 *full, u64 *empty, int stages,
         }
         for (int i = 0; i < n_extra; ++i) mbar_init(&extra[i], extra_count);
         for (int i = 0; i < n_extra2; ++i) mbar_init(&extra2[i], extra2_count);
+        mbar_init(&edone[0], n_cons_warps);                  // edge-balanced split: consumer warps done
+        mbar_init(&edone[1], 1);                             // ... and the pieces of the first node are ready
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -294,20 +419,21 @@ __device__ __forceinline__ void init_barriers(u64 *full, u64 *empty, int stages,
 template <int STAGES, int CG, int CPT, int NP, int H>
 __device__ __forceinline__ void fwd_consume(const float *smem, u64 *full, u64 *empty, u64 *red_full, u64 *red_free,
                                             float *red, const float *__restrict__ Y, const int *__restrict__ rowptr,
-                                            float *__restrict__ out, long long n_nodes, long long nb, int grp,
-                                            int u0, int lane) {
+                                            float *__restrict__ out, long long n_nodes, long long n_edges,
+                                            long long nb, const ERange &er, float *part, int *flags, u64 *edone,
+                                            int grp, int u0, int lane) {
     constexpr int GT = MUL / CPT;
     constexpr u32 STAGE_F = W_DIM + X_DIM + 20;
     u32 it = 0, node_it = 0;
     long long chunk = blockIdx.x, n0, n1;
-    while (next_chunk(chunk, nb, n_nodes, n0, n1))
+    while (next_chunk(chunk, nb, n_nodes, er, n0, n1))
     for (long long n = n0; n < n1; ++n, ++node_it) {
         float acc[CPT][ORR];
 #pragma unroll
         for (int q = 0; q < CPT; ++q)
 #pragma unroll
             for (int i = 0; i < ORR; ++i) acc[q][i] = 0.0f;
-        const int p0 = rowptr[n], p1 = rowptr[n + 1];
+        const int p0 = (int)max((long long)rowptr[n], er.q0), p1 = (int)min((long long)rowptr[n + 1], er.q1);
         for (int p = p0; p < p1; ++p, ++it) {
             if (it % CG != (u32)grp) continue;  // ring position it is always group it % CG's (STAGES % CG == 0)
             const u32 st = it % STAGES, ph = (it / STAGES) & 1;
@@ -335,10 +461,14 @@ __device__ __forceinline__ void fwd_consume(const float *smem, u64 *full, u64 *e
             return;
         }
         if (grp == 0) {
+            float *row = row_of_node(out, part, n, OUT_DIM, rowptr, er);
 #pragma unroll
-            for (int q = 0; q < CPT; ++q) fwd_store<H>(out + n * OUT_DIM, u0 + q * GT, acc[q]);
+            for (int q = 0; q < CPT; ++q) fwd_store<H>(row, u0 + q * GT, acc[q]);
         }
     }
+    if (nb < 0)
+        finish_pieces<CG * NP * GT>(out, part, flags, OUT_DIM, rowptr, er, n_edges, &edone[0], &edone[1],
+                                    (int)threadIdx.x, lane);
 }
 
 // CTA = CG consumer groups x NP parts x GT = MUL / CPT threads (+ the producer warp).  Thread (grp, part, u0) computes,
@@ -349,7 +479,7 @@ __global__ void MMK_FWD_BOUNDS(CG * NP * (MUL / CPT) + 32)
 mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ senders, float *__restrict__ out, long long n_nodes,
-                    long long n_edges, long long nb) {
+                    long long n_edges, long long nb, float *pieces, int *piece_flags) {
     static_assert(NP == 1 || CG == 1, "a forward split over parts runs one consumer group");
     constexpr int GT = MUL / CPT;                   // threads of one part of a group
     constexpr u32 NCW = GT / 32;                    // warps of one part
@@ -360,9 +490,12 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     u64 *empty = full + STAGES;
     u64 *red_full = empty + STAGES;                 // [2]
     u64 *red_free = red_full + 2;                   // [2]
-    float *red = reinterpret_cast<float *>(red_free + 2);   // [2][CG-1][ORR][MUL]
+    u64 *edone = red_free + 2;                      // [2] edge-balanced split
+    float *red = reinterpret_cast<float *>(edone + 2);      // [2][CG-1][ORR][MUL]
     const int tid = threadIdx.x;
-    init_barriers(full, empty, STAGES, NP * NCW, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW);
+    init_barriers(full, empty, STAGES, NP * NCW, red_full, 2, CG > 1 ? (CG - 1) * NCW : 1, red_free, 2, NCW, edone,
+                  CG * NP * NCW);
+    const ERange er = edge_range(rowptr, n_nodes, n_edges, nb);
 
     if (tid >= CG * GTH) {                          // producer warp
 #ifdef MMK_TEST_STALL
@@ -378,8 +511,8 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
             if constexpr (Y_TMA) bulk_g2s(stage + W_DIM + X_DIM, Y + e * YD, YD * 4, bar);
         };
         long long chunk = blockIdx.x, n0, n1;
-        while (next_chunk(chunk, nb, n_nodes, n0, n1)) {
-            if (!produce<STAGES>(rowptr, eids, senders, n0, n1, n_nodes, n_edges, full, empty, it, issue)) {
+        while (next_chunk(chunk, nb, n_nodes, er, n0, n1)) {
+            if (!produce<STAGES>(rowptr, eids, senders, n0, n1, er, n_nodes, n_edges, full, empty, it, issue)) {
                 if ((tid & 31) == 0) atomicExch(&mmk_status, 1);
                 break;
             }
@@ -388,13 +521,13 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     }
 
     const int grp = tid / GTH, part = (tid % GTH) / GT, u0 = tid % GT, lane = tid & 31;
-    if (part == 0) fwd_consume<STAGES, CG, CPT, NP, 0>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, nb, grp, u0, lane);
+    if (part == 0) fwd_consume<STAGES, CG, CPT, NP, 0>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, n_edges, nb, er, pieces, piece_flags, edone, grp, u0, lane);
     if constexpr (NP > 1) {
-        if (part == 1) fwd_consume<STAGES, CG, CPT, NP, 1>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, nb, grp, u0, lane);
+        if (part == 1) fwd_consume<STAGES, CG, CPT, NP, 1>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, n_edges, nb, er, pieces, piece_flags, edone, grp, u0, lane);
     }
     if constexpr (NP > 2) {
-        if (part == 2) fwd_consume<STAGES, CG, CPT, NP, 2>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, nb, grp, u0, lane);
-        if (part == 3) fwd_consume<STAGES, CG, CPT, NP, 3>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, nb, grp, u0, lane);
+        if (part == 2) fwd_consume<STAGES, CG, CPT, NP, 2>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, n_edges, nb, er, pieces, piece_flags, edone, grp, u0, lane);
+        if (part == 3) fwd_consume<STAGES, CG, CPT, NP, 3>(smem, full, empty, red_full, red_free, red, Y, rowptr, out, n_nodes, n_edges, nb, er, pieces, piece_flags, edone, grp, u0, lane);
     }
 }
 
@@ -407,14 +540,15 @@ __device__ __forceinline__ void bwd_consume(const float *smem, u64 *full, u64 *e
                                             float *red, float *part_buf, int *arrived, const float *__restrict__ x,
                                             const float *__restrict__ Y, const int *__restrict__ rowptr,
                                             float *__restrict__ gx, float *__restrict__ gY, float *__restrict__ gW,
-                                            long long n_nodes, long long n_edges, long long nb, int grp, int lg,
-                                            int u0, int gwarp, int lane) {
+                                            long long n_nodes, long long n_edges, long long nb, const ERange &er,
+                                            float *part, int *flags, u64 *edone, int grp, int lg, int u0, int gwarp,
+                                            int lane) {
     constexpr int GT = MUL / CPT;
     constexpr u32 GW = NP * (GT / 32);
     constexpr u32 STAGE_F = W_DIM + OUT_DIM + 20;
     u32 it = 0, node_it = 0;
     long long chunk = blockIdx.x, n0, n1;
-    while (next_chunk(chunk, nb, n_nodes, n0, n1))
+    while (next_chunk(chunk, nb, n_nodes, er, n0, n1))
     for (long long s = n0; s < n1; ++s, ++node_it) {
         float xs[CPT][XR], gxa[CPT][XR];
 #pragma unroll
@@ -423,7 +557,7 @@ __device__ __forceinline__ void bwd_consume(const float *smem, u64 *full, u64 *e
 #pragma unroll
             for (int i = 0; i < XR; ++i) gxa[q][i] = 0.0f;
         }
-        const int p0 = rowptr[s], p1 = rowptr[s + 1];
+        const int p0 = (int)max((long long)rowptr[s], er.q0), p1 = (int)min((long long)rowptr[s + 1], er.q1);
         for (int p = p0; p < p1; ++p, ++it) {
             if (it % CG != (u32)grp) continue;  // ring position it is always group it % CG's (STAGES % CG == 0)
             const u32 st = it % STAGES, ph = (it / STAGES) & 1;
@@ -481,10 +615,14 @@ __device__ __forceinline__ void bwd_consume(const float *smem, u64 *full, u64 *e
             return;
         }
         if (gx != nullptr && lg == 0) {
+            float *row = row_of_node(gx, part, s, X_DIM, rowptr, er);
 #pragma unroll
-            for (int q = 0; q < CPT; ++q) store_x(gx + s * X_DIM, u0 + q * GT, gxa[q]);
+            for (int q = 0; q < CPT; ++q) store_x(row, u0 + q * GT, gxa[q]);
         }
     }
+    if (nb < 0 && gx != nullptr)
+        finish_pieces<CG * NP * GT>(gx, part, flags, X_DIM, rowptr, er, n_edges, &edone[0], &edone[1],
+                                    (int)threadIdx.x, lane);
 }
 
 // Same CTA shape.  The CG*NP (group, part) pairs are the "logical groups" of the gx sum at the end of a sender: each
@@ -494,7 +632,8 @@ __global__ void MMK_BWD_BOUNDS(CG * NP * (MUL / CPT) + 32)
 mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
                     const float *__restrict__ g, const int *__restrict__ rowptr, const int *__restrict__ eids,
                     const long long *__restrict__ receivers, float *__restrict__ gx, float *__restrict__ gY,
-                    float *__restrict__ gW, long long n_nodes, long long n_edges, long long nb) {
+                    float *__restrict__ gW, long long n_nodes, long long n_edges, long long nb, float *pieces,
+                    int *piece_flags) {
     constexpr int GT = MUL / CPT;                   // threads of one part of a group
     constexpr u32 NCW = GT / 32;                    // warps of one part
     constexpr int GTH = NP * GT;                    // threads of one group
@@ -505,12 +644,15 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     u64 *empty = full + STAGES;
     u64 *red_full = empty + STAGES;                 // [2]   gx hand-over between logical groups
     u64 *red_free = red_full + 2;                   // [2]
-    float *part_buf = reinterpret_cast<float *>(red_free + 2);      // [STAGES][GW][16] gY partials of each warp
+    u64 *edone = red_free + 2;                      // [2] edge-balanced split
+    float *part_buf = reinterpret_cast<float *>(edone + 2);         // [STAGES][GW][16] gY partials of each warp
     int *arrived = reinterpret_cast<int *>(part_buf + STAGES * GW * 16);   // [STAGES] warps done with the stage's gY
     float *red = reinterpret_cast<float *>(arrived + STAGES);       // [2][CG*NP-1][XR][MUL]
     const int tid = threadIdx.x;
     for (int i = tid; i < STAGES; i += blockDim.x) arrived[i] = 0;
-    init_barriers(full, empty, STAGES, GW, red_full, 2, CG * NP > 1 ? (CG * NP - 1) * NCW : 1, red_free, 2, NCW);
+    init_barriers(full, empty, STAGES, GW, red_full, 2, CG * NP > 1 ? (CG * NP - 1) * NCW : 1, red_free, 2, NCW, edone,
+                  CG * NP * NCW);
+    const ERange er = edge_range(rowptr, n_nodes, n_edges, nb);
 
     if (tid >= CG * GTH) {
 #ifdef MMK_TEST_STALL
@@ -526,8 +668,8 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
             if constexpr (Y_TMA) bulk_g2s(stage + W_DIM + OUT_DIM, Y + e * YD, YD * 4, bar);
         };
         long long chunk = blockIdx.x, n0, n1;
-        while (next_chunk(chunk, nb, n_nodes, n0, n1)) {
-            if (!produce<STAGES>(rowptr, eids, receivers, n0, n1, n_nodes, n_edges, full, empty, it, issue)) {
+        while (next_chunk(chunk, nb, n_nodes, er, n0, n1)) {
+            if (!produce<STAGES>(rowptr, eids, receivers, n0, n1, er, n_nodes, n_edges, full, empty, it, issue)) {
                 if ((tid & 31) == 0) atomicExch(&mmk_status, 3);
                 break;
             }
@@ -538,12 +680,12 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
     const int grp = tid / GTH, part = (tid % GTH) / GT, u0 = tid % GT;
     const int gwarp = (tid % GTH) >> 5, lane = tid & 31;   // warp index within the group (all parts)
     const int lg = grp * NP + part;                        // logical group of the gx sum
-    if (part == 0) bwd_consume<STAGES, CG, CPT, NP, 0>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, grp, lg, u0, gwarp, lane);
+    if (part == 0) bwd_consume<STAGES, CG, CPT, NP, 0>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, er, pieces, piece_flags, edone, grp, lg, u0, gwarp, lane);
     if constexpr (NP > 1) {
-        if (part == 1) bwd_consume<STAGES, CG, CPT, NP, 1>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, grp, lg, u0, gwarp, lane);
+        if (part == 1) bwd_consume<STAGES, CG, CPT, NP, 1>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, er, pieces, piece_flags, edone, grp, lg, u0, gwarp, lane);
     }
     if constexpr (NP > 2) {
-        if (part == 2) bwd_consume<STAGES, CG, CPT, NP, 2>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, grp, lg, u0, gwarp, lane);
-        if (part == 3) bwd_consume<STAGES, CG, CPT, NP, 3>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, grp, lg, u0, gwarp, lane);
+        if (part == 2) bwd_consume<STAGES, CG, CPT, NP, 2>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, er, pieces, piece_flags, edone, grp, lg, u0, gwarp, lane);
+        if (part == 3) bwd_consume<STAGES, CG, CPT, NP, 3>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, er, pieces, piece_flags, edone, grp, lg, u0, gwarp, lane);
     }
 }

@@ -8,6 +8,11 @@
 // error at the float32 level (~1e-6 relative for these K) instead of TF32's ~1e-3.  B is a constant operand here (the
 // weights of a layer), so the caller passes it already split (mmk_tf32_split); A is split while it is staged.
 //
+// Accumulation: the tensor cores add into the float32 accumulator without round-to-nearest, so its error grows with
+// the number of MMAs that add into it (measured: ~7x a float32 SIMT product at K = 1280 with one accumulator).  The
+// kernel therefore keeps 2 x KS accumulators in tensor memory: the hi.hi products and the two small cross products
+// in separate ones, and the K chunks dealt round-robin over KS such pairs; the epilogue adds them on the CUDA cores.
+//
 // One CTA of 4 warps computes a 128 x BN tile of C (BN = 64 / 128 / 256 columns of tensor memory, lane = row):
 //   * every K chunk of 32 (one 128-byte row of each operand) is staged by all 128 threads into a ring of STAGES
 //     shared-memory stages in the 128B-swizzled K-major layout the MMA descriptors describe (16-byte piece c of row r
@@ -15,8 +20,12 @@
 //   * thread 0 issues, per chunk, 4 K-steps x 3 products of tcgen05.mma (M = 128, N = BN, K = 8) and commits them to
 //     the stage's mbarrier; the threads stage the next chunk meanwhile and wait on that barrier only before they
 //     overwrite the stage;
-//   * the epilogue reads the accumulator back with tcgen05.ld (warp w: lanes 32w..32w+31, 32 columns at a time) and
-//     stores the rows.
+//   * the epilogue reads the accumulator back with tcgen05.ld (warp w: lanes 32w..32w+31, 16 columns at a time),
+//     stages the tile in shared memory and stores whole rows (coalesced);
+//   * the next chunk is in flight while a chunk is split and multiplied: its A in registers, its (already split) B
+//     by cp.async straight into the swizzled tiles;
+//   * outputs with fewer tiles than SMs split K over a third grid dimension; partial tiles go to a caller-provided
+//     workspace and the last CTA of a tile adds them in split order (deterministic).
 // Every wait is bounded; on expiry the kernel records a status (mmk_gemm_status), still waits (bounded) for its MMAs,
 // frees its tensor memory and returns.
 
@@ -107,55 +116,117 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, float4 v) {
                  : "memory");
 }
 
-// Stage rows [0, ROWS) x floats [k0, k0 + 32) of a K-major matrix (row stride ld floats, `rows` valid rows, K valid
-// columns) into the swizzled tile at `hi` (and its TF32 split at hi / lo when SPLIT).  Warp w, instruction i: rows
-// 16*i + 4*w + lane/8, 16-byte piece lane % 8.  Rows or columns out of range are zero.
-template <int ROWS, bool SPLIT>
-__device__ __forceinline__ void stage_rows(const float *__restrict__ src, long long ld, long long rows, int K, int k0,
-                                           uint32_t hi, uint32_t lo) {
+// A chunk (ROWS rows x 32 floats of K) of a K-major matrix: warp w, instruction i loads rows 16*i + 4*w + lane/8,
+// 16-byte piece lane % 8 (coalesced: 8 lanes read one 128-byte row).  Rows or columns out of range are zero.
+template <int ROWS>
+struct Chunk {
+    float4 v[ROWS / 16];
+};
+
+template <int ROWS>
+__device__ __forceinline__ void load_chunk(Chunk<ROWS> &ch, const float *__restrict__ src, long long ld,
+                                           long long rows, int K, int k0) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int k = k0 + 4 * (lane & 7);
+#pragma unroll
+    for (int i = 0; i < ROWS / 16; ++i) {
+        const int r = 16 * i + 4 * warp + (lane >> 3);
+        ch.v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < rows && k < K) ch.v[i] = __ldg(reinterpret_cast<const float4 *>(src + (long long)r * ld + k));
+    }
+}
+
+// Byte offset of 16-byte piece c of row r in a 128B-swizzled K-major tile.
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) { return (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4); }
+
+// Split a staged chunk into its TF32 high and low parts, stored in the swizzled tiles at hi / lo.
+template <int ROWS>
+__device__ __forceinline__ void store_split(const Chunk<ROWS> &ch, uint32_t hi, uint32_t lo) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c = lane & 7;
+#pragma unroll
+    for (int i = 0; i < ROWS / 16; ++i) {
+        const int r = 16 * i + 4 * warp + (lane >> 3);
+        const float4 v = ch.v[i];
+        const float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+        const float4 l = make_float4(tf32_rna(v.x - h.x), tf32_rna(v.y - h.y), tf32_rna(v.z - h.z), tf32_rna(v.w - h.w));
+        st_shared_v4(hi + sw128_off(r, c), h);
+        st_shared_v4(lo + sw128_off(r, c), l);
+    }
+}
+
+// Copy a chunk of an already split operand straight into its swizzled tile with cp.async (16 bytes per thread and
+// instruction, no registers); out-of-range pieces are zero-filled (src-size 0).
+template <int ROWS>
+__device__ __forceinline__ void async_chunk(uint32_t dst, const float *__restrict__ src, long long ld, long long rows,
+                                            int K, int k0) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c = lane & 7;
     const int k = k0 + 4 * c;
-    constexpr int IT = ROWS / 16;
-    float4 v[IT];
 #pragma unroll
-    for (int i = 0; i < IT; ++i) {
+    for (int i = 0; i < ROWS / 16; ++i) {
         const int r = 16 * i + 4 * warp + (lane >> 3);
-        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (r < rows && k < K) v[i] = __ldg(reinterpret_cast<const float4 *>(src + (long long)r * ld + k));
+        const bool in = r < rows && k < K;
+        const float *g = in ? src + (long long)r * ld + k : src;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + sw128_off(r, c)), "l"(g),
+                     "r"(in ? 16 : 0)
+                     : "memory");
     }
+}
+
+// C tile: thread (warp w, lane l) holds row 32w + l of the accumulator; the tile goes through shared memory (row
+// stride BN + 4 floats: the 16-byte stores of a warp fall on distinct banks) so that global stores are whole rows.
+template <int BN>
+__device__ __forceinline__ void tile_to_smem(float *tile, const float (&v)[16], int j) {
+    const int row = threadIdx.x;
 #pragma unroll
-    for (int i = 0; i < IT; ++i) {
-        const int r = 16 * i + 4 * warp + (lane >> 3);
-        const uint32_t off = (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
-        if constexpr (SPLIT) {
-            const float4 h = make_float4(tf32_rna(v[i].x), tf32_rna(v[i].y), tf32_rna(v[i].z), tf32_rna(v[i].w));
-            const float4 l = make_float4(tf32_rna(v[i].x - h.x), tf32_rna(v[i].y - h.y), tf32_rna(v[i].z - h.z),
-                                         tf32_rna(v[i].w - h.w));
-            st_shared_v4(hi + off, h);
-            st_shared_v4(lo + off, l);
-        } else {
-            st_shared_v4(hi + off, v[i]);
+    for (int q = 0; q < 16; q += 4)
+        *reinterpret_cast<float4 *>(tile + row * (BN + 4) + j + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+}
+
+// Rows [0, 128) x columns [0, ncols) of the smem tile -> dst (row stride ld), warp w writing rows w, w + 4, ...
+template <int BN>
+__device__ __forceinline__ void smem_to_rows(float *__restrict__ dst, long long ld, const float *tile, long long rows,
+                                             int ncols) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int r = warp; r < BM && r < rows; r += 4) {
+        const float *src = tile + r * (BN + 4);
+        float *d = dst + (long long)r * ld;
+        for (int c = 4 * lane; c < ncols; c += 128) {
+            if (c + 4 <= ncols) {
+                *reinterpret_cast<float4 *>(d + c) = *reinterpret_cast<const float4 *>(src + c);
+            } else {
+                for (int q = c; q < ncols; ++q) d[q] = src[q];
+            }
         }
     }
 }
 
-template <int BN, int STAGES>
+// grid (M tiles, N tiles, K splits).  With K splits > 1 every CTA writes its partial tile to ws (tile-major,
+// [split][tile][128][BN]) and the CTA that arrives last for a tile (counter per tile, back to zero afterwards) adds
+// the partials in split order -- deterministic whichever CTA is last.
+template <int BN, int STAGES, int KS>
 __global__ void __launch_bounds__(128, 1)
 k_gemm_tf32x3(const float *__restrict__ A, long long lda, const float *__restrict__ Bhi,
               const float *__restrict__ Blo, long long ldb, float *__restrict__ C, long long ldc, long long M, int N,
-              int K) {
+              int K, float *__restrict__ ws, int *__restrict__ counters) {
     static_assert(BN == 64 || BN == 128 || BN == 256, "tensor-memory columns: a power of two, M = 128 needs N % 16");
+    static_assert(2 * KS * BN <= 512, "2 x KS accumulators of BN columns in the 512 columns of tensor memory");
+    constexpr uint32_t TCOLS = 2 * KS * BN;
     constexpr uint32_t A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;
     constexpr uint32_t STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static_assert(STAGES * STAGE_BYTES >= BM * (BN + 4) * 4, "the C tile reuses the operand stages");
     constexpr uint32_t IDESC = idesc_tf32<BM, BN>();
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                             ~static_cast<uintptr_t>(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + STAGES);
+    int *last_flag = reinterpret_cast<int *>(tmem_slot + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const long long m0 = (long long)blockIdx.x * BM;
     const int n0 = blockIdx.y * BN;
+    const int nk_all = (K + BK - 1) / BK, splits = gridDim.z;
+    const int kz0 = (int)((long long)nk_all * blockIdx.z / splits), kz1 = (int)((long long)nk_all * (blockIdx.z + 1) / splits);
+    const int nk = kz1 - kz0;                                 // chunks of this CTA
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
@@ -163,7 +234,7 @@ k_gemm_tf32x3(const float *__restrict__ A, long long lda, const float *__restric
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(BN)
+                     "r"(TCOLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -175,18 +246,35 @@ k_gemm_tf32x3(const float *__restrict__ A, long long lda, const float *__restric
     const float *Ab = A + m0 * lda;
     const float *Bh = Bhi + (long long)n0 * ldb, *Bl = Blo + (long long)n0 * ldb;
     const long long rows_a = M - m0, rows_b = (long long)N - n0;
-    const int nk = (K + BK - 1) / BK;
     bool ok = true;
     int committed = -1;                                       // last chunk whose MMAs thread 0 committed
-    for (int kc = 0; kc < nk; ++kc) {
-        const int s = kc % STAGES;
+    Chunk<BM> a_next;
+    if (nk > 0) {                                             // prologue: chunk 0 in flight
+        const uint32_t base = smem_u32(smem);
+        async_chunk<BN>(base + 2 * A_BYTES, Bh, ldb, rows_b, K, kz0 * BK);
+        async_chunk<BN>(base + 2 * A_BYTES + B_BYTES, Bl, ldb, rows_b, K, kz0 * BK);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        load_chunk<BM>(a_next, Ab, lda, rows_a, K, kz0 * BK);
+    }
+    for (int i = 0; i < nk; ++i) {
+        const int s = i % STAGES;
         const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-        // the stage is free once the MMAs of chunk kc - STAGES (its previous use) have completed
-        const bool free_ = kc < STAGES || mbar_wait(&bars[s], (uint32_t)((kc / STAGES) - 1) & 1u);
-        if (free_) {
-            stage_rows<BM, true>(Ab, lda, rows_a, K, kc * BK, base, base + A_BYTES);
-            stage_rows<BN, false>(Bh, ldb, rows_b, K, kc * BK, base + 2 * A_BYTES, 0);
-            stage_rows<BN, false>(Bl, ldb, rows_b, K, kc * BK, base + 2 * A_BYTES + B_BYTES, 0);
+        store_split<BM>(a_next, base, base + A_BYTES);        // this chunk's A (its stage was freed before its B)
+        bool free_ = true;
+        if (i + 1 < nk) {                                     // next chunk: B by cp.async, A into registers
+            const int s1 = (i + 1) % STAGES;
+            const uint32_t b1 = smem_u32(smem + s1 * STAGE_BYTES);
+            // stage s1 is free once the MMAs of its previous use (chunk i + 1 - STAGES) have completed
+            free_ = i + 1 < STAGES || mbar_wait(&bars[s1], (uint32_t)(((i + 1) / STAGES) - 1) & 1u);
+            if (free_) {
+                async_chunk<BN>(b1 + 2 * A_BYTES, Bh, ldb, rows_b, K, (kz0 + i + 1) * BK);
+                async_chunk<BN>(b1 + 2 * A_BYTES + B_BYTES, Bl, ldb, rows_b, K, (kz0 + i + 1) * BK);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            load_chunk<BM>(a_next, Ab, lda, rows_a, K, (kz0 + i + 1) * BK);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");   // this chunk's B has landed
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");    // generic writes -> tensor-core reads
         tc_fence_before();
@@ -197,51 +285,90 @@ k_gemm_tf32x3(const float *__restrict__ A, long long lda, const float *__restric
         if (tid == 0) {
             tc_fence_after();
             const uint32_t a_hi = base, a_lo = base + A_BYTES, b_hi = base + 2 * A_BYTES, b_lo = b_hi + B_BYTES;
+            const uint32_t big = tmem + (uint32_t)(2 * (i % KS) * BN), small = big + BN;   // this chunk's pair
+            const bool first = i < KS;
 #pragma unroll
             for (int j = 0; j < BK / 8; ++j) {
-                const uint32_t o = 32u * j;
-                mma_tf32(tmem, sw128_desc(a_lo + o), sw128_desc(b_hi + o), IDESC, (kc > 0 || j > 0) ? 1u : 0u);
-                mma_tf32(tmem, sw128_desc(a_hi + o), sw128_desc(b_lo + o), IDESC, 1u);
-                mma_tf32(tmem, sw128_desc(a_hi + o), sw128_desc(b_hi + o), IDESC, 1u);
+                const uint32_t o = 32u * j, acc = (first && j == 0) ? 0u : 1u;
+                mma_tf32(small, sw128_desc(a_lo + o), sw128_desc(b_hi + o), IDESC, acc);
+                mma_tf32(small, sw128_desc(a_hi + o), sw128_desc(b_lo + o), IDESC, 1u);
+                mma_tf32(big, sw128_desc(a_hi + o), sw128_desc(b_hi + o), IDESC, acc);
             }
             mma_commit(&bars[s]);
         }
-        committed = kc;
+        committed = i;
         __syncwarp();
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     // the barrier of the last committed chunk tracks every MMA issued before it
     bool done = committed < 0 ||
                 mbar_wait(&bars[committed % STAGES], (uint32_t)(committed / STAGES) & 1u);
     done = __syncthreads_and(done) != 0;
     tc_fence_after();
+    float *tile = reinterpret_cast<float *>(smem);            // the operand stages are free now
     if (ok && done) {
-        const long long row = m0 + warp * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const int npairs = nk < KS ? nk : KS;               // accumulator pairs that received MMAs
 #pragma unroll 1
         for (int j = 0; j < BN; j += 16) {
-            float v[16];
-            tmem_ld16(lane_base + (uint32_t)j, v);
-            const int col = n0 + j;
-            if (row < M && col < N) {
-                float *dst = C + row * ldc + col;
-                if (col + 16 <= N) {
+            float v[16], w[16], t[16];
 #pragma unroll
-                    for (int q = 0; q < 16; q += 4)
-                        *reinterpret_cast<float4 *>(dst + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-                } else {
-                    for (int q = 0; q < N - col; ++q) dst[q] = v[q];
-                }
+            for (int q = 0; q < 16; ++q) v[q] = w[q] = 0.0f;
+#pragma unroll 1
+            for (int q = 0; q < npairs; ++q) {
+                tmem_ld16(lane_base + (uint32_t)(2 * q * BN + BN + j), t);   // small cross products
+#pragma unroll
+                for (int r = 0; r < 16; ++r) w[r] += t[r];
+                tmem_ld16(lane_base + (uint32_t)(2 * q * BN + j), t);        // hi.hi products
+#pragma unroll
+                for (int r = 0; r < 16; ++r) v[r] += t[r];
             }
+#pragma unroll
+            for (int r = 0; r < 16; ++r) v[r] += w[r];
+            tile_to_smem<BN>(tile, v, j);
         }
     } else if (tid == 0) {
         atomicExch(&g_status, done ? 1 : 2);
     }
     tc_fence_before();
-    __syncthreads();
+    const bool good = __syncthreads_and(ok && done) != 0;     // the tile is complete in shared memory
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
     }
+    if (!good) return;
+    const int ncols = min(BN, N - n0);
+    if (splits == 1) {
+        smem_to_rows<BN>(C + m0 * ldc + n0, ldc, tile, rows_a, ncols);
+        return;
+    }
+    const long long n_tiles = (long long)gridDim.x * gridDim.y;
+    const long long tile_id = (long long)blockIdx.y * gridDim.x + blockIdx.x;
+    smem_to_rows<BN>(ws + ((long long)blockIdx.z * n_tiles + tile_id) * BM * BN, BN, tile, BM, BN);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) *last_flag = atomicAdd(&counters[tile_id], 1) == splits - 1;
+    __syncthreads();
+    if (!*last_flag) return;
+    __threadfence();
+    for (int r = warp; r < BM && r < rows_a; r += 4) {        // partials added in split order
+        for (int c = 4 * lane; c < ncols; c += 128) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int z = 0; z < splits; ++z) {
+                const float4 p = __ldcg(reinterpret_cast<const float4 *>(
+                    ws + ((long long)z * n_tiles + tile_id) * BM * BN + (long long)r * BN + c));
+                acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+            }
+            float *d = C + (m0 + r) * ldc + n0 + c;
+            if (c + 4 <= ncols) {
+                *reinterpret_cast<float4 *>(d) = acc;
+            } else {
+                const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+                for (int q = 0; q < ncols - c; ++q) d[q] = a4[q];
+            }
+        }
+    }
+    if (tid == 0) counters[tile_id] = 0;                      // ready for the next launch
 }
 
 __global__ void k_tf32_split(const float *__restrict__ x, float *__restrict__ hi, float *__restrict__ lo,
@@ -256,6 +383,14 @@ __global__ void k_tf32_split(const float *__restrict__ x, float *__restrict__ hi
 template <int BN, int STAGES>
 constexpr int smem_bytes() {
     return STAGES * (2 * BM * BK * 4 + 2 * BN * BK * 4) + STAGES * 8 + 16 + 1024;
+}
+
+// K splits of a launch: enough CTAs to cover the SMs when the output has few tiles, at least 4 chunks per split.
+inline int gemm_splits(long long tiles, int nk, int sms) {
+    if (tiles >= sms || nk < 8) return 1;
+    long long s = (sms + tiles - 1) / tiles;
+    s = s < nk / 4 ? s : nk / 4;
+    return (int)(s < 1 ? 1 : (s > 16 ? 16 : s));
 }
 
 }  // namespace mmk_gemm

@@ -37,6 +37,22 @@ def tf32_split_host(t: torch.Tensor):
     return torch.from_numpy(hi.copy()), torch.from_numpy(lo.copy())
 
 
+_WORKSPACE = {}          # device -> zero-initialised uint8 tensor (K-split partial tiles and tile counters)
+
+
+def _workspace(M, N, K, device):
+    """The per-device workspace of the K-split launches, grown on demand (zero-filled: the kernel leaves its tile
+    counters at zero after every call, so a buffer is reused as is)."""
+    need = int(_lib.lib().mmk_gemm_workspace_bytes(M, N, K))
+    if need == 0:
+        return None, 0
+    ws = _WORKSPACE.get(device)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(need, dtype=torch.uint8, device=device)
+        _WORKSPACE[device] = ws
+    return ws, ws.numel()
+
+
 def matmul_nt(a: torch.Tensor, b_hi: torch.Tensor, b_lo: torch.Tensor, out: torch.Tensor | None = None):
     """a [M, K] . b^T with b = b_hi + b_lo [N, K] (split by ``tf32_split``) -> [M, N], float32."""
     if a.dtype != torch.float32 or not a.is_cuda:
@@ -48,8 +64,9 @@ def matmul_nt(a: torch.Tensor, b_hi: torch.Tensor, b_lo: torch.Tensor, out: torc
         raise ValueError(f'operand shapes {tuple(a.shape)} x {tuple(b_hi.shape)}^T do not match')
     if out is None:
         out = torch.empty(M, N, device=a.device, dtype=torch.float32)
+    ws, nbytes = _workspace(M, N, K, a.device)
     _lib.call('mmk_gemm_tf32x3', _lib.ptr(a), a.stride(0), _lib.ptr(b_hi), _lib.ptr(b_lo), b_hi.stride(0),
-              _lib.ptr(out), out.stride(0), M, N, K, _lib.stream_of(a))
+              _lib.ptr(out), out.stride(0), M, N, K, _lib.ptr(ws), nbytes, _lib.stream_of(a))
     return out
 
 

@@ -5,8 +5,9 @@ host.
 
 A cell list over wrapped fractional coordinates (float64): atoms binned by a CSR build, one warp per atom walks the
 neighbouring (bin, periodic image) pairs, a scan places every atom's edges and a per-atom rank sort orders them.  The
-capacity is fixed per ``DeviceNeighborList``, rows past the pair count are padding edges (node 0 to itself, far
-away), and nothing synchronises with the host, so a step that rebuilds the graph can be captured in a CUDA graph.
+capacity is fixed per ``DeviceNeighborList``, rows past the pair count are padding edges (padding edge k: node k mod N
+to itself, far away), and nothing synchronises with the host, so a step that rebuilds the graph can be captured in a
+CUDA graph.
 """
 from __future__ import annotations
 

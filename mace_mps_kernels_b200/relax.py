@@ -1,24 +1,21 @@
-"""Structure relaxation loop on the GPU: limited-memory BFGS over energy + force calls at a fixed padded graph size.
+"""Structure relaxation loop: limited-memory BFGS over energy + force calls at a fixed padded graph size.
 
 This drives the patched model the way a geometry optimiser drives a MACE calculator (50 E+F calls
-of an 89-element model on an Au13 cluster over CeO2(111)), without leaving the device between calls:
+of an 89-element model on an Au13 cluster over CeO2(111)):
 
-* the graph is rebuilt every step by ``DeviceNeighborList`` (float64 positions, fixed edge capacity, padding edges
-  carry zero messages), so the shapes never change;
+* the graph is rebuilt every step on the GPU by ``DeviceNeighborList`` (float64 positions, fixed edge capacity,
+  padding edges carry zero messages), so the shapes never change;
 * the E+F call is a replay of one CUDA graph (``GraphedEnergyForces``) when ``graphed`` is set, else the eager model;
-* the optimiser state (positions, the last ``memory`` position and gradient differences) stays in device memory; a
-  step reads one scalar back (the curvature test below).
+* the optimiser runs on the host in float64, as atomistic optimisers do: one force read-back and one position upload
+  per step.
 
-The optimiser is L-BFGS with a constant initial inverse Hessian ``gamma = 1 / alpha`` and a step scaled so that no
-atom moves further than ``maxstep`` (Angstrom), the variant common in atomistic codes.  The product of the inverse
-Hessian with the gradient uses the compact representation of Byrd, Nocedal and Schnabel (Math. Programming 63, 1994,
-eq. 3.1): with the last k pairs as rows of S and Y, R = upper triangle of S Y^T and D its diagonal,
-    H g = gamma g + S^T u - gamma Y^T p,   p = R^-1 (S g),   u = R^-T ((D + gamma Y Y^T) p - gamma Y g),
-a fixed number of small kernels per step instead of the two-loop recursion's 2k.  A pair is kept only if s.y > 0
-(one scalar read back per step).
+The optimiser is the two-loop L-BFGS recursion (Nocedal and Wright, Numerical Optimization, algorithm 7.4) with a
+constant initial inverse Hessian ``1 / alpha`` and a step scaled so that no atom moves further than ``maxstep``
+(Angstrom), the variant common in atomistic codes.  Curvature pairs with s.y <= 0 are not stored.
 """
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 from . import standin
@@ -42,17 +39,22 @@ class Relaxation:
         idx = torch.tensor([z_index[int(z)] for z in structure.numbers])
         self.node_attrs = torch.nn.functional.one_hot(idx, len(z_table)).float().to(self.device)
         self.nl = DeviceNeighborList(structure.cell, structure.pbc, r_max, n, capacity, self.device)
-        self.pos = torch.as_tensor(structure.positions, dtype=torch.float64, device=self.device).clone()
+        self.pos = np.array(structure.positions, dtype=np.float64)              # host, float64 (the optimiser's)
+        self.pos_host = torch.zeros(n, 3, dtype=torch.float64).pin_memory()
+        self.pos_dev = torch.zeros(n, 3, dtype=torch.float64, device=self.device)
+        self.forces_host = torch.zeros(n, 3, dtype=torch.float32).pin_memory()
         self.batch_index = torch.zeros(n, dtype=torch.long, device=self.device)
         self.graphed = None
         if graphed:
             self.graphed = GraphedEnergyForces(model, self._batch())
-        self.S, self.Y = [], []                            # curvature pairs, oldest first (float64, device)
+        self.S, self.Y = [], []                            # curvature pairs, oldest first
         self.r0 = self.g0 = None
 
     def _batch(self):
-        ei, sh, _ = self.nl(self.pos)
-        return {'positions': self.pos.float(), 'node_attrs': self.node_attrs, 'edge_index': ei, 'shifts': sh,
+        self.pos_host.numpy()[:] = self.pos
+        self.pos_dev.copy_(self.pos_host, non_blocking=True)
+        ei, sh, _ = self.nl(self.pos_dev)
+        return {'positions': self.pos_dev.float(), 'node_attrs': self.node_attrs, 'edge_index': ei, 'shifts': sh,
                 'batch': self.batch_index, 'num_graphs': 1}
 
     def energy_forces(self):
@@ -65,34 +67,38 @@ class Relaxation:
         out = self.model(b, compute_force=True, training=False)
         return out['energy'].detach(), out['forces'].detach()
 
-    def _inv_hessian_times(self, g):
-        gam = self.h0
-        if not self.S:
-            return gam * g
-        S, Y = torch.stack(self.S), torch.stack(self.Y)       # [k, 3n]
-        SY = S @ Y.T
-        R = torch.triu(SY)
-        p = torch.linalg.solve_triangular(R, (S @ g)[:, None], upper=True)
-        t = (torch.diag(torch.diagonal(SY)) + gam * (Y @ Y.T)) @ p - gam * (Y @ g)[:, None]
-        u = torch.linalg.solve_triangular(R.T, t, upper=False)
-        return gam * g + (S.T @ u)[:, 0] - gam * (Y.T @ p)[:, 0]
+    def _direction(self, g):
+        """-H g by the two-loop recursion over the stored pairs (newest first, then oldest first)."""
+        q = g.copy()
+        alphas = []
+        for s, y in zip(reversed(self.S), reversed(self.Y)):
+            rho = 1.0 / float(y @ s)
+            a = rho * float(s @ q)
+            q -= a * y
+            alphas.append((rho, a))
+        z = self.h0 * q
+        for (s, y), (rho, a) in zip(zip(self.S, self.Y), reversed(alphas)):
+            z += s * (a - rho * float(y @ z))
+        return -z
 
     def step(self):
-        """One E+F call and one L-BFGS update of the positions; returns (energy, forces) of the call."""
+        """One E+F call and one L-BFGS update of the positions; returns (energy, forces) of the call (device)."""
         E, F = self.energy_forces()
-        g = -F.double().reshape(-1)                       # gradient of the energy
+        self.forces_host.copy_(F)                          # the one read-back of the step (synchronises)
+        g = -self.forces_host.numpy().astype(np.float64).reshape(-1)
         r = self.pos.reshape(-1)
         if self.r0 is not None:
             s, y = r - self.r0, g - self.g0
-            if float(torch.dot(s, y)) > 0.0:              # keep only pairs of positive curvature
+            if float(s @ y) > 0.0:                         # keep only pairs of positive curvature
                 self.S.append(s)
                 self.Y.append(y)
                 if len(self.S) > self.memory:
                     del self.S[0], self.Y[0]
-        dr = -self._inv_hessian_times(g).reshape(-1, 3)
-        longest = dr.norm(dim=1).max()
-        dr = dr * torch.clamp(self.maxstep / longest.clamp_min(1e-300), max=1.0)
-        self.r0, self.g0 = r.clone(), g
+        dr = self._direction(g).reshape(-1, 3)
+        longest = float(np.sqrt((dr * dr).sum(1)).max())
+        if longest > self.maxstep:
+            dr *= self.maxstep / longest
+        self.r0, self.g0 = r.copy(), g
         self.pos = self.pos + dr
         return E, F
 
@@ -104,7 +110,7 @@ class Relaxation:
         for t in range(calls):
             E, F = self.step()
             energies[t] = E.double().reshape(-1)[0]
-        return energies, F
+        return energies, F.clone()
 
 
 def ceo2_au13_workload(device, seed=0, r_max=6.0, capacity_margin=1.3):

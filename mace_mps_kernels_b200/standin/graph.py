@@ -99,7 +99,8 @@ def atoms_to_graph(st, z_table, r_max, dtype=torch.float32):
 
 
 def pad_edges(g, n_edges, far=1.0e3):
-    """Pad a graph to exactly ``n_edges`` with self-edges of node 0 shifted by ``far`` A (beyond any cutoff).
+    """Pad a graph to exactly ``n_edges`` with self-edges shifted by ``far`` A (beyond any cutoff), padding edge k on
+    node k mod N (spread over the nodes, so that no node's CSR segment grows with the padding).
 
     A padding edge has a finite direction (harmonics are defined) and a length past r_max, so the polynomial cutoff
     makes its radial features, its per-edge weights and hence its message and every gradient through it exactly 0."""
@@ -110,7 +111,8 @@ def pad_edges(g, n_edges, far=1.0e3):
         return g
     k = n_edges - E
     g = dict(g)
-    g['edge_index'] = torch.cat([g['edge_index'], torch.zeros(2, k, dtype=torch.long)], 1)
+    v = torch.arange(k, dtype=torch.long) % max(int(g['num_nodes']), 1)
+    g['edge_index'] = torch.cat([g['edge_index'], torch.stack([v, v])], 1)
     pad = torch.zeros(k, 3, dtype=g['shifts'].dtype)
     pad[:, 0] = far
     g['shifts'] = torch.cat([g['shifts'], pad], 0)

@@ -154,12 +154,13 @@ def test_gemm_entry_points_validate_arguments():
     from mace_mps_kernels_b200 import _lib
     L = _lib.lib()
     p = ctypes.c_void_p(16)                                    # never dereferenced: validation fails first
-    assert L.mmk_gemm_tf32x3(p, 64, p, p, 64, p, 64, -1, 8, 64, None) == _lib.MMK_ERR_INVALID
-    assert L.mmk_gemm_tf32x3(p, 64, p, p, 64, p, 64, 10, 8, 62, None) == _lib.MMK_ERR_INVALID     # K % 4
-    assert L.mmk_gemm_tf32x3(p, 32, p, p, 64, p, 64, 10, 8, 64, None) == _lib.MMK_ERR_INVALID     # lda < K
-    assert L.mmk_gemm_tf32x3(ctypes.c_void_p(20), 64, p, p, 64, p, 64, 10, 8, 64, None) == _lib.MMK_ERR_INVALID
-    assert L.mmk_gemm_tf32x3(None, 64, p, p, 64, p, 64, 10, 8, 64, None) == _lib.MMK_ERR_INVALID
-    assert L.mmk_gemm_tf32x3(p, 64, p, p, 64, p, 64, 0, 8, 64, None) == _lib.MMK_OK                # empty
+    assert L.mmk_gemm_tf32x3(p, 64, p, p, 64, p, 64, -1, 8, 64, None, 0, None) == _lib.MMK_ERR_INVALID
+    assert L.mmk_gemm_tf32x3(p, 64, p, p, 64, p, 64, 10, 8, 62, None, 0, None) == _lib.MMK_ERR_INVALID   # K % 4
+    assert L.mmk_gemm_tf32x3(p, 32, p, p, 64, p, 64, 10, 8, 64, None, 0, None) == _lib.MMK_ERR_INVALID   # lda < K
+    assert L.mmk_gemm_tf32x3(ctypes.c_void_p(20), 64, p, p, 64, p, 64, 10, 8, 64, None, 0, None) == _lib.MMK_ERR_INVALID
+    assert L.mmk_gemm_tf32x3(None, 64, p, p, 64, p, 64, 10, 8, 64, None, 0, None) == _lib.MMK_ERR_INVALID
+    assert L.mmk_gemm_tf32x3(p, 64, p, p, 64, p, 64, 0, 8, 64, None, 0, None) == _lib.MMK_OK              # empty
+    assert L.mmk_gemm_workspace_bytes(5218, 64, 1280) > 0 and L.mmk_gemm_workspace_bytes(5218, 1280, 64) == 0
     assert L.mmk_tf32_split(p, p, p, -1, None) == _lib.MMK_ERR_INVALID
 
 

@@ -54,7 +54,9 @@ def test_device_neighbor_list_matches_host(cuda, name):
     assert np.array_equal(ei[0, :E].cpu().numpy(), i) and np.array_equal(ei[1, :E].cpu().numpy(), j)
     ref = (Sh.astype(np.float64) @ st.cell).astype(np.float32)
     assert np.abs(sh[:E].cpu().numpy() - ref).max() <= 1e-5 * max(1.0, np.abs(ref).max())
-    assert bool((ei[:, E:] == 0).all()) and bool((sh[E:, 0] == 1000.0).all()) and bool((sh[E:, 1:] == 0).all())
+    pad = torch.arange(ei.shape[1] - E, device=ei.device) % len(st)        # padding edge k: node k mod N
+    assert bool((ei[0, E:] == pad).all()) and bool((ei[1, E:] == pad).all())
+    assert bool((sh[E:, 0] == 1000.0).all()) and bool((sh[E:, 1:] == 0).all())
 
 
 def test_overflow_is_reported(cuda):

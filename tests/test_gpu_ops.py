@@ -50,6 +50,7 @@ def test_conv_fwd_bwd_matches_oracle(cuda, hidden, lmax, N, E):
 # Alternative launch plans (the layer-creation overrides used for tuning): channels per consumer thread, group
 # counts, ring sizes and the per-term backward body.
 PLAN_VARIANTS = [
+    {'MMK_CONV_EDGE_SPLIT': '0'},              # node ranges per CTA on small graphs (no pieces)
     {'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2'},
     {'MMK_CONV_FWD_CPT': '4', 'MMK_CONV_BWD_CPT': '4', 'MMK_CONV_FWD_CG': '8', 'MMK_CONV_BWD_CG': '8'},
     {'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2', 'MMK_CONV_FWD_CG': '8', 'MMK_CONV_BWD_CG': '8'},
@@ -212,3 +213,35 @@ def test_double_backward_raises_on_ops(cuda):
     with pytest.raises(RuntimeError, match='double backward'):
         (g,) = torch.autograd.grad(out.square().sum(), x, create_graph=True)
         torch.autograd.grad(g.sum(), x)
+
+
+@pytest.mark.parametrize('hidden,N,E', [('128x0e+128x1o', 5, 2000), ('128x0e+128x1o+128x2e', 168, 5218),
+                                        ('128x0e', 40, 6000)])
+def test_conv_edge_split_repeatable_and_equal_to_node_ranges(cuda, monkeypatch, hidden, N, E):
+    """Small graphs run the edge-balanced split (pieces of straddling nodes summed in CTA order): launches repeat
+    bit for bit (the per-CTA flags are back at zero after every launch), and the result equals the node-range split
+    within float32 rounding."""
+    from mace_mps_kernels_b200.conv import CudaConvTP
+    torch.manual_seed(1)
+    tp = helpers.conv_tp(hidden, 3).to(cuda)
+    ei = helpers.random_graph(N, E, seed=7).to(cuda)
+    x = torch.randn(N, tp.irreps_in1.dim, device=cuda, requires_grad=True)
+    Y = torch.randn(E, tp.irreps_in2.dim, device=cuda, requires_grad=True)
+    W = torch.randn(E, tp.weight_numel, device=cuda, requires_grad=True)
+
+    def run(op):
+        out = op(x, Y, W, ei)
+        g = torch.ones_like(out)
+        return (out.detach(),) + torch.autograd.grad(out, (x, Y, W), g)
+
+    monkeypatch.setenv('MMK_CONV_EDGE_SPLIT', '1')
+    op = CudaConvTP(tp)
+    first = run(op)
+    for _ in range(3):
+        again = run(op)
+        assert all(torch.equal(a, b) for a, b in zip(first, again))
+    assert op.status() == 0
+    monkeypatch.setenv('MMK_CONV_EDGE_SPLIT', '0')
+    nodes = run(CudaConvTP(tp))
+    for a, b, name in zip(first, nodes, ('out', 'gx', 'gY', 'gW')):
+        close(a, b.double().cpu().numpy(), what=name)
