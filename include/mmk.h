@@ -296,7 +296,8 @@ MMK_API int mmk_tf32_split(const float *x, float *hi, float *lo, int64_t n, void
  * C + i*ldc); B given split (mmk_tf32_split).  K, lda, ldb, ldc multiples of 4; A, B_hi, B_lo, C 16-byte aligned.
  * Tiles of 128 rows x 64/128/256 columns, accumulator in tensor memory.  Outputs with fewer tiles than SMs split K
  * over several CTAs when a workspace of mmk_gemm_workspace_bytes(M, N, K) bytes (16-byte aligned, zero-filled before
- * its first use; every call leaves its counters at zero) is given; with workspace NULL (or too small) they do not.
+ * its first use; its first 1 KB holds tile counters that every call leaves at zero, so one workspace of the largest
+ * size serves calls of every shape) is given; with workspace NULL (or too small) they do not.
  * Deterministic either way.  Calls that share a workspace must be ordered on the GPU. */
 MMK_API size_t mmk_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 MMK_API int mmk_gemm_tf32x3(const float *A, int64_t lda, const float *B_hi, const float *B_lo, int64_t ldb, float *C,

@@ -110,6 +110,25 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, u32 bytes, 
                  : "memory");
 }
 
+// The same copy with an L2 eviction-priority hint (the per-edge rows W[e] and Y[e] are read exactly once: streamed
+// with evict_first so that they do not push the gathered node rows, which other edges read again, out of L2).
+__device__ __forceinline__ u64 l2_evict_first() {
+    u64 p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void bulk_g2s_stream(void *dst, const void *src, u32 bytes, u64 *bar, u64 pol) {
+#if MMK_L2_HINT
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
+        : "memory");
+#else
+    bulk_g2s(dst, src, bytes, bar);
+#endif
+}
+
 // Reduce v[0..15] over the 32 lanes of a warp; afterwards lanes 2j and 2j+1 both hold the full sum of v[j].
 __device__ __forceinline__ float warp_transpose_reduce16(float (&v)[16]) {
     const int lane = threadIdx.x & 31;
@@ -502,13 +521,14 @@ mmk_conv_fwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         return;
 #endif
         u32 it = 0;
+        const u64 pol = l2_evict_first();
         auto issue = [&](u32 st, long long e, long long s, u64 *bar) {
             float *stage = smem + st * STAGE_F;
             *reinterpret_cast<long long *>(stage + W_DIM + X_DIM + 16) = e;       // released by the arrive below
             mbar_arrive_expect_tx(bar, (W_DIM + X_DIM) * 4 + (Y_TMA ? YD * 4 : 0));
-            bulk_g2s(stage, W + e * W_DIM, W_DIM * 4, bar);
+            bulk_g2s_stream(stage, W + e * W_DIM, W_DIM * 4, bar, pol);
             bulk_g2s(stage + W_DIM, x + s * X_DIM, X_DIM * 4, bar);
-            if constexpr (Y_TMA) bulk_g2s(stage + W_DIM + X_DIM, Y + e * YD, YD * 4, bar);
+            if constexpr (Y_TMA) bulk_g2s_stream(stage + W_DIM + X_DIM, Y + e * YD, YD * 4, bar, pol);
         };
         long long chunk = blockIdx.x, n0, n1;
         while (next_chunk(chunk, nb, n_nodes, er, n0, n1)) {
@@ -659,13 +679,14 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         return;
 #endif
         u32 it = 0;
+        const u64 pol = l2_evict_first();
         auto issue = [&](u32 st, long long e, long long r, u64 *bar) {
             float *stage = smem + st * STAGE_F;
             *reinterpret_cast<long long *>(stage + W_DIM + OUT_DIM + 16) = e;     // released by the arrive below
             mbar_arrive_expect_tx(bar, (W_DIM + OUT_DIM) * 4 + (Y_TMA ? YD * 4 : 0));
-            bulk_g2s(stage, W + e * W_DIM, W_DIM * 4, bar);
+            bulk_g2s_stream(stage, W + e * W_DIM, W_DIM * 4, bar, pol);
             bulk_g2s(stage + W_DIM, g + r * OUT_DIM, OUT_DIM * 4, bar);
-            if constexpr (Y_TMA) bulk_g2s(stage + W_DIM + OUT_DIM, Y + e * YD, YD * 4, bar);
+            if constexpr (Y_TMA) bulk_g2s_stream(stage + W_DIM + OUT_DIM, Y + e * YD, YD * 4, bar, pol);
         };
         long long chunk = blockIdx.x, n0, n1;
         while (next_chunk(chunk, nb, n_nodes, er, n0, n1)) {
