@@ -254,10 +254,92 @@ def time_cases(cases, reps, flush):
             out[f'{tag}_hot_us'] = e0.elapsed_time(e1) * 1e3 / reps
             if c['kind'] == 'conv':
                 out[f'{tag}_gbs'] = c[f'{tag}_bytes'] / out[f'{tag}_us'] * 1e-3
-            else:
+            elif f'{tag}_flops' in c:
                 out[f'{tag}_tflops'] = c[f'{tag}_flops'] / out[f'{tag}_us'] * 1e-6
         res.append(out)
     return res
+
+
+def other_cases(model, batch):
+    """The other library ops of one E+F call (equivariant linears and skip connections, the radial MLP's hidden
+    layers and its tensor-core last layer), each with the inputs it saw, as (fwd, bwd) launch closures."""
+    from mace_mps_kernels_b200 import gemm as G
+    from mace_mps_kernels_b200.dense import CudaFullyConnectedNet, CudaLinear, CudaSkipTP
+    from mace_mps_kernels_b200.symmetric import element_groups
+    calls = []
+
+    def hook(mod, args, kwargs, out):
+        calls.append((mod, [a.detach() if torch.is_tensor(a) else a for a in args]))
+
+    hs = [m.register_forward_hook(hook, with_kwargs=True) for m in model.modules()
+          if isinstance(m, (CudaLinear, CudaSkipTP, CudaFullyConnectedNet))]
+    e_and_f(model, batch)
+    for h in hs:
+        h.remove()
+    cases = []
+    for k, (mod, args) in enumerate(calls):
+        x = args[0].contiguous()
+        if isinstance(mod, CudaFullyConnectedNet):
+            E, L = x.shape[0], len(mod.hidden_widths) - 1
+            h = torch.empty(E, mod.hidden_widths[-1], device=x.device)
+            z = torch.empty(E * sum(mod.hidden_widths[1:]), device=x.device)
+            gh = torch.randn_like(h)
+            gx = torch.empty_like(x)
+            P = _lib.ptr
+            st = _lib.stream_of(x)
+            fwd = lambda x=x, h=h, z=z, mod=mod, E=E, L=L, st=st: _lib.call(
+                'mmk_mlp_fwd', P(x), E, L, mod.widths_c(), P(mod.w_hidden), mod.scale, P(h), P(z), st)
+            bwd = lambda gh=gh, z=z, gx=gx, mod=mod, E=E, L=L, st=st: _lib.call(
+                'mmk_mlp_bwd', P(gh), E, L, mod.widths_c(), P(mod.w_hidden_t), P(z), mod.scale, P(gx), st)
+            flops = sum(2 * E * a * b for a, b in zip(mod.hidden_widths[:-1], mod.hidden_widths[1:]))
+            cases.append(dict(op=f'mlp_hidden[{k}]', kind='mlp', N=E, fwd=fwd, bwd=bwd, fwd_flops=flops,
+                              bwd_flops=flops, keep=(x, h, z, gh, gx)))
+            lin = mod.last
+            W = torch.empty(E, lin.n + lin.n_pad, device=x.device)
+            gW = torch.randn_like(W)
+            gh2 = torch.empty(E, lin.k + lin.k_pad, device=x.device)
+            hp = torch.randn(E, lin.k + lin.k_pad, device=x.device)
+            fwd = lambda hp=hp, lin=lin, W=W: G.matmul_nt(hp, lin.wt_hi, lin.wt_lo, out=W)
+            bwd = lambda gW=gW, lin=lin, gh2=gh2: G.matmul_nt(gW, lin.w_hi, lin.w_lo, out=gh2)
+            f = 2 * E * lin.k * lin.n
+            cases.append(dict(op=f'mlp_last_gemm[{k}]', kind='gemm', N=E, fwd=fwd, bwd=bwd, fwd_flops=f,
+                              bwd_flops=f, keep=(hp, W, gW, gh2)))
+            continue
+        groups = None
+        if isinstance(mod, CudaSkipTP):
+            _, erow, perm = element_groups(args[1].contiguous())
+            groups = (perm, erow, mod.n_elem)
+        N = x.shape[0]
+        out = torch.empty(N, mod.out_dim, device=x.device)
+        g = torch.randn_like(out)
+        gx = torch.empty_like(x)
+        fwd = lambda mod=mod, x=x, out=out, groups=groups: mod._launch(mod.fwd, x, mod.in_dim, out, mod.out_dim, groups)
+        bwd = lambda mod=mod, g=g, gx=gx, groups=groups: mod._launch(mod.bwd, g, mod.out_dim, gx, mod.in_dim, groups)
+        cases.append(dict(op=f'{type(mod).__name__}[{k}]', kind='block_linear', N=N, fwd=fwd, bwd=bwd,
+                          keep=(x, out, g, gx, groups)))
+    return cases
+
+
+def step_breakdown(conv_sc_ops, other_ops):
+    """Measured time per library-op family in one E+F step (sum over its launches of the cold per-launch times) and
+    the family with the largest share."""
+    fam = {}
+    for o in conv_sc_ops + other_ops:
+        name = {'conv': 'conv_tp (mmk_conv_fwd/bwd_kernel)', 'sc': 'symmetric contraction (mmk_sc_fwd/bwd_kernel)',
+                'block_linear': 'equivariant linears + skip (k_block_linear)',
+                'mlp': 'radial MLP hidden layers (k_mlp_fwd/bwd)',
+                'gemm': 'radial MLP last layer (k_gemm_tf32x3)'}[o['kind']]
+        f = fam.setdefault(name, {'us': 0.0, 'launches': 0})
+        f['us'] += o['fwd_us'] + o['bwd_us']
+        f['launches'] += 2
+    total = sum(f['us'] for f in fam.values())
+    for f in fam.values():
+        f['share'] = round(f['us'] / total, 4)
+        f['us'] = round(f['us'], 1)
+    top = max(fam, key=lambda k: fam[k]['us'])
+    return {'families': fam, 'top': top, 'library_us_sum': round(total, 1),
+            'timing': "each op's forward and backward launch on the step's own inputs, cold (1 GiB L2 flush before "
+                      "each launch), summed per family; launch gaps and PyTorch glue kernels not included"}
 
 
 def step_cases(model, batch):
@@ -525,6 +607,8 @@ def main():
     big_flush = torch.empty(1024 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     flush = lambda: flush_l2(big_flush)
     ops = time_cases(step_cases(model, batch), a.op_reps, flush)
+    other_ops = time_cases(other_cases(model, batch), max(3, a.op_reps // 2), flush)
+    breakdown = step_breakdown(ops, other_ops)
     hbm, hbm_kind = peaks()
 
     def conv_roof(o, note, traffic=None):
@@ -542,8 +626,10 @@ def main():
 
     pair = ('mmk_conv_fwd_kernel', 'mmk_conv_bwd_kernel')
     dom = max((o for o in ops if o['kind'] == 'conv'), key=lambda o: o['fwd_us'] + o['bwd_us'])
-    roofline = conv_roof(dom, 'dominant kernel of the timed E+F step; its data fits in L2, so it is latency-bound '
-                              '(cold: L2 flushed before the launch)',
+    roofline = conv_roof(dom, 'the hot path\'s dominant kernel in the timed E+F step (the conv layer with the '
+                              'longest forward + backward); its data fits in L2, so it is latency-bound (cold: L2 '
+                              'flushed before the launch).  The largest library share of the step is named in '
+                              'step_breakdown.top',
                          traffic=measured_traffic(pair, dom['N'], dom['E'], dom['_dims']))
     large, roof_large, fp32 = None, None, None
     if not a.no_large and rank == 0:
@@ -584,6 +670,8 @@ def main():
             'roofline': roofline, 'cpu_baseline': cpu, 'gpu_launches': launches, 'clocks': clk.summary(),
             'eager_ms_per_step': round(eager_ms, 3),
             'ops': [rounded(o) for o in ops],
+            'step_breakdown': breakdown,
+            'ops_other': [rounded(o) for o in other_ops],
             'roofline_large': roof_large,
             'ops_large': None if large is None else dict(large, ops=[rounded(o) for o in large['ops']]),
         }

@@ -290,11 +290,33 @@ __device__ __forceinline__ void finish_pieces(float *out, float *part, int *flag
         return;
     }
     if (!pieces_ok) return;                                  // thread 0 gave up on the flags: leave the row
-    float *dst = out + er.n_first * (long long)row;
-    for (int i = ct; i < row; i += NC) {
-        float v = 0.0f;
-        for (long long k = c_first; k < c; ++k) v += __ldcg(part + 2 * k * row + i);
-        dst[i] = v + __ldcg(part + (2 * c + 1) * row + i);
+    // the row = earlier pieces in CTA order, then this CTA's own; rows are whole float4 (MUL is a multiple of 32) and
+    // each thread sums 8 float4 at a time so that the loads of a piece are in flight together
+    float4 *dst = reinterpret_cast<float4 *>(out + er.n_first * (long long)row);
+    const float4 *p4 = reinterpret_cast<const float4 *>(part);
+    const int row4 = row / 4;
+#pragma unroll 1
+    for (int b0 = ct; b0 < row4; b0 += 8 * NC) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+        for (long long k = c_first; k <= c; ++k) {
+            const long long slot = k < c ? 2 * k : 2 * c + 1;
+            float4 t[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int i = b0 + u * NC;
+                t[u] = i < row4 ? __ldcg(p4 + slot * row4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                v[u].x += t[u].x; v[u].y += t[u].y; v[u].z += t[u].z; v[u].w += t[u].w;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (b0 + u * NC < row4) dst[b0 + u * NC] = v[u];
     }
 }
 

@@ -351,20 +351,35 @@ k_gemm_tf32x3(const float *__restrict__ A, long long lda, const float *__restric
     __syncthreads();
     if (!*last_flag) return;
     __threadfence();
-    for (int r = warp; r < BM && r < rows_a; r += 4) {        // partials added in split order
-        for (int c = 4 * lane; c < ncols; c += 128) {
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int z = 0; z < splits; ++z) {
-                const float4 p = __ldcg(reinterpret_cast<const float4 *>(
-                    ws + ((long long)z * n_tiles + tile_id) * BM * BN + (long long)r * BN + c));
-                acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+    // partials added in split order; each thread sums 8 float4 of the tile at a time (independent loads in flight)
+    constexpr int PER = BM * BN / 4 / 128;                    // float4 of the tile per thread
+    const float4 *part4 = reinterpret_cast<const float4 *>(ws + tile_id * BM * BN);
+    const long long split_stride4 = n_tiles * BM * BN / 4;
+#pragma unroll 1
+    for (int b0 = 0; b0 < PER; b0 += 8) {
+        float4 acc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+        for (int z = 0; z < splits; ++z) {
+            float4 t[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) t[u] = __ldcg(part4 + z * split_stride4 + tid + (b0 + u) * 128);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                acc[u].x += t[u].x; acc[u].y += t[u].y; acc[u].z += t[u].z; acc[u].w += t[u].w;
             }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int q = (tid + (b0 + u) * 128) * 4, r = q / BN, c = q % BN;
+            if (r >= rows_a || c >= ncols) continue;
             float *d = C + (m0 + r) * ldc + n0 + c;
             if (c + 4 <= ncols) {
-                *reinterpret_cast<float4 *>(d) = acc;
+                *reinterpret_cast<float4 *>(d) = acc[u];
             } else {
-                const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-                for (int q = 0; q < ncols - c; ++q) d[q] = a4[q];
+                const float a4[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+                for (int k = 0; k < ncols - c; ++k) d[k] = a4[k];
             }
         }
     }

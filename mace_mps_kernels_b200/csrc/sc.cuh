@@ -189,16 +189,22 @@ mmk_sc_fwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, con
     }
     const int j = warp % SC_CC;
     u32 it = 0;
+    // the node features of the next unit are loaded while the current unit's terms are evaluated
+    Unit nx = unit_of(blockIdx.x, perm, erow, n_elem, n_nodes);
+    float xn[NELL];
+    if (nx.ok && nx.node >= 0 && nx.c < CH) load_feat(x + (nx.node * CH + nx.c) * NELL, xn);
     for (long long u = blockIdx.x; u < n_units; u += gridDim.x, ++it) {
-        const Unit un = unit_of(u, perm, erow, n_elem, n_nodes);
+        const Unit un = nx;
         if (!un.ok) break;
         const bool active = un.node >= 0 && un.c < CH;
         float xv[NELL], acc[OUTM];
-        if (active) {
-            load_feat(x + (un.node * CH + un.c) * NELL, xv);
-        } else {
 #pragma unroll
-            for (int i = 0; i < NELL; ++i) xv[i] = 0.0f;
+        for (int i = 0; i < NELL; ++i) xv[i] = active ? xn[i] : 0.0f;
+        if (u + gridDim.x < n_units) {
+            nx = unit_of(u + gridDim.x, perm, erow, n_elem, n_nodes);
+            if (nx.ok && nx.node >= 0 && nx.c < CH) load_feat(x + (nx.node * CH + nx.c) * NELL, xn);
+        } else {
+            nx.ok = false;
         }
 #pragma unroll
         for (int i = 0; i < OUTM; ++i) acc[i] = 0.0f;
@@ -230,19 +236,30 @@ mmk_sc_bwd_kernel(const float *__restrict__ x, const int *__restrict__ perm, con
     }
     const int j = warp % SC_CC;
     u32 it = 0;
+    // the node features and output gradients of the next unit are loaded while the current unit is evaluated
+    Unit nx = unit_of(blockIdx.x, perm, erow, n_elem, n_nodes);
+    float xn[NELL], gn[OUTM];
+    if (nx.ok && nx.node >= 0 && nx.c < CH) {
+        load_feat(x + (nx.node * CH + nx.c) * NELL, xn);
+        sc_load_grad(g, nx.node, nx.c, gn);
+    }
     for (long long u = blockIdx.x; u < n_units; u += gridDim.x, ++it) {
-        const Unit un = unit_of(u, perm, erow, n_elem, n_nodes);
+        const Unit un = nx;
         if (!un.ok) break;
         const bool active = un.node >= 0 && un.c < CH;
         float xv[NELL], gv[OUTM], d[NELL];
-        if (active) {
-            load_feat(x + (un.node * CH + un.c) * NELL, xv);
-            sc_load_grad(g, un.node, un.c, gv);
+#pragma unroll
+        for (int i = 0; i < NELL; ++i) xv[i] = active ? xn[i] : 0.0f;
+#pragma unroll
+        for (int i = 0; i < OUTM; ++i) gv[i] = active ? gn[i] : 0.0f;
+        if (u + gridDim.x < n_units) {
+            nx = unit_of(u + gridDim.x, perm, erow, n_elem, n_nodes);
+            if (nx.ok && nx.node >= 0 && nx.c < CH) {
+                load_feat(x + (nx.node * CH + nx.c) * NELL, xn);
+                sc_load_grad(g, nx.node, nx.c, gn);
+            }
         } else {
-#pragma unroll
-            for (int i = 0; i < NELL; ++i) xv[i] = 0.0f;
-#pragma unroll
-            for (int i = 0; i < OUTM; ++i) gv[i] = 0.0f;
+            nx.ok = false;
         }
 #pragma unroll
         for (int i = 0; i < NELL; ++i) d[i] = 0.0f;

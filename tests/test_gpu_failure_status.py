@@ -44,15 +44,16 @@ def test_conv_wait_timeout_sets_status_and_returns(cuda, monkeypatch):
     W = torch.randn(E, op.spec.w_dim, device=cuda, requires_grad=True)
     out = op(x, Y, W, ei)
     torch.cuda.synchronize()                       # the launch completes although no copy ever lands
-    # 2: a forward consumer's ring wait ran out (9: a consumer group's hand-over wait, if it got there first)
+    # 2: a forward consumer's ring wait ran out (9: a consumer group's hand-over wait, 10 / 11: the edge-balanced
+    # split's waits for the pieces of a straddling node, if one of those gave up last)
     st = op.status()
-    assert st in (2, 9), f'forward timeout status expected, got {st}'
+    assert st in (2, 9, 10, 11), f'forward timeout status expected, got {st}'
     assert op.status(reset=True) == st
     assert op.status() == 0
     torch.autograd.grad(out, (x, Y, W), torch.ones_like(out))
     torch.cuda.synchronize()
     st = op.status(reset=True)
-    assert st in (4, 9), f'backward timeout status expected, got {st}'
+    assert st in (4, 9, 10, 11), f'backward timeout status expected, got {st}'
 
     # the context is still usable: a normally built layer gives the oracle's result
     tp, good = _conv_layer(monkeypatch, stalled=False)
