@@ -216,10 +216,13 @@ def sc_case(mod, x, attrs, name):
     gx = torch.empty_like(x)
     fwd = lambda: _lib.call('mmk_sc_fwd', mod.handle, P(x), P(perm), P(erow), ne, P(mod.T), P(o), N, st)
     bwd = lambda: _lib.call('mmk_sc_bwd', mod.handle, P(x), P(perm), P(erow), ne, P(mod.T), P(g), P(gx), N, st)
+    from mace_mps_kernels_b200.symmetric import executed_flops
     ff, fb = mod.spec.flops()
+    ef, eb = executed_flops(mod.spec)
     C = mod.spec.C
     return dict(op=name, kind='sc', N=N, terms=mod.spec.n_terms, fwd=fwd, bwd=bwd, fwd_flops=ff * N * C,
-                bwd_flops=fb * N * C, keep=(mod, o, g, gx, erow, perm))
+                bwd_flops=fb * N * C, fwd_exec_flops=ef * N * C, bwd_exec_flops=eb * N * C,
+                keep=(mod, o, g, gx, erow, perm))
 
 
 def time_cases(cases, reps, flush):
@@ -256,6 +259,8 @@ def time_cases(cases, reps, flush):
                 out[f'{tag}_gbs'] = c[f'{tag}_bytes'] / out[f'{tag}_us'] * 1e-3
             elif f'{tag}_flops' in c:
                 out[f'{tag}_tflops'] = c[f'{tag}_flops'] / out[f'{tag}_us'] * 1e-6
+                if f'{tag}_exec_flops' in c:        # what the generated code executes (fewer than the term count)
+                    out[f'{tag}_exec_tflops'] = c[f'{tag}_exec_flops'] / out[f'{tag}_us'] * 1e-6
         res.append(out)
     return res
 
@@ -280,6 +285,8 @@ def other_cases(model, batch):
     for k, (mod, args) in enumerate(calls):
         x = args[0].contiguous()
         if isinstance(mod, CudaFullyConnectedNet):
+            if not mod.fused:
+                continue
             E, L = x.shape[0], len(mod.hidden_widths) - 1
             h = torch.empty(E, mod.hidden_widths[-1], device=x.device)
             z = torch.empty(E * sum(mod.hidden_widths[1:]), device=x.device)
@@ -645,6 +652,8 @@ def main():
         for o in large['ops'] + ops:
             if o['kind'] == 'sc':
                 o['fp32_peak_tflops'] = round(fp32, 1)
+                for tag in ('fwd', 'bwd'):          # executed work against the measured FP32 peak
+                    o[f'{tag}_exec_frac_of_fp32_peak'] = round(o[f'{tag}_exec_tflops'] / fp32, 4)
 
     extras = {}
     if not a.no_extras:

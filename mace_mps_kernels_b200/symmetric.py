@@ -156,6 +156,21 @@ class SCSpec:
         return fwd, bwd
 
 
+def executed_flops(spec):
+    """(forward, backward) floating-point operations the generated term code executes per (node, channel): it is
+    straight-line code, so every ``fmaf`` (2 flops) and every binary ``*`` or ``+`` of two floats (1 flop) in the
+    bodies runs exactly once.  Fewer than ``flops()``, which counts the terms as the reference evaluates them."""
+    import re
+    src = source(spec)
+    res = []
+    for name in ('sc_fwd_body', 'sc_bwd_body'):
+        i = src.index('void ' + name)
+        body = src[i:src.index('\n}\n', i)]
+        body = re.sub(r'\[[^\]]*\]', '[]', body)                 # index expressions are not float arithmetic
+        res.append(2 * body.count('fmaf(') + len(re.findall(r'[\w\]\)] [*+] [\w(]', body)))
+    return tuple(res)
+
+
 _ELEM_CACHE = []
 
 

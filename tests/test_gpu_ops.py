@@ -51,6 +51,7 @@ def test_conv_fwd_bwd_matches_oracle(cuda, hidden, lmax, N, E):
 # counts, ring sizes and the per-term backward body.
 PLAN_VARIANTS = [
     {'MMK_CONV_EDGE_SPLIT': '0'},              # node ranges per CTA on small graphs (no pieces)
+    {'MMK_CONV_EDGE_SPLIT': '1'},              # edge-balanced ranges in both directions (default: backward only)
     {'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2'},
     {'MMK_CONV_FWD_CPT': '4', 'MMK_CONV_BWD_CPT': '4', 'MMK_CONV_FWD_CG': '8', 'MMK_CONV_BWD_CG': '8'},
     {'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2', 'MMK_CONV_FWD_CG': '8', 'MMK_CONV_BWD_CG': '8'},
