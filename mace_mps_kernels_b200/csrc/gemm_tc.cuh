@@ -13,14 +13,15 @@
 // kernel therefore keeps 2 x KS accumulators in tensor memory: the hi.hi products and the two small cross products
 // in separate ones, and the K chunks dealt round-robin over KS such pairs; the epilogue adds them on the CUDA cores.
 //
-// One CTA of 4 warps computes a 128 x BN tile of C (BN = 64 / 128 / 256 columns of tensor memory, lane = row):
-//   * every K chunk of 32 (one 128-byte row of each operand) is staged by all 128 threads into a ring of STAGES
+// One CTA of 8 warps computes a 128 x BN tile of C (BN = 64 / 128 / 256 columns of tensor memory, lane = row):
+//   * every K chunk of 32 (one 128-byte row of each operand) is staged by all 256 threads into a ring of STAGES
 //     shared-memory stages in the 128B-swizzled K-major layout the MMA descriptors describe (16-byte piece c of row r
 //     stored at r*128 + ((c ^ (r % 8)) * 16); 4 rows per warp instruction, coalesced 128-byte row reads);
 //   * thread 0 issues, per chunk, 4 K-steps x 3 products of tcgen05.mma (M = 128, N = BN, K = 8) and commits them to
 //     the stage's mbarrier; the threads stage the next chunk meanwhile and wait on that barrier only before they
 //     overwrite the stage;
-//   * the epilogue reads the accumulator back with tcgen05.ld (warp w: lanes 32w..32w+31, 16 columns at a time),
+//   * the epilogue reads the accumulator back with tcgen05.ld (warps w and w + 4: lanes 32w..32w+31, each half of
+//     the columns, 16 at a time),
 //     stages the tile in shared memory and stores whole rows (coalesced);
 //   * the next chunk is in flight while a chunk is split and multiplied: its A in registers, its (already split) B
 //     by cp.async straight into the swizzled tiles;
@@ -34,6 +35,8 @@ namespace mmk_gemm {
 __device__ int g_status;
 
 constexpr int BM = 128;                 // tile rows = MMA M = tensor-memory lanes
+constexpr int NW = 8;                   // warps per CTA (two per tensor-memory lane quadrant)
+constexpr int NT = 32 * NW;             // threads per CTA
 constexpr int BK = 32;                  // K chunk: 32 floats = one 128-byte swizzle row
 constexpr long long WAIT_BUDGET = 2000000000LL;   // clock64 cycles (~1 s)
 
@@ -116,11 +119,11 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, float4 v) {
                  : "memory");
 }
 
-// A chunk (ROWS rows x 32 floats of K) of a K-major matrix: warp w, instruction i loads rows 16*i + 4*w + lane/8,
+// A chunk (ROWS rows x 32 floats of K) of a K-major matrix: warp w, instruction i loads rows 4*NW*i + 4*w + lane/8,
 // 16-byte piece lane % 8 (coalesced: 8 lanes read one 128-byte row).  Rows or columns out of range are zero.
 template <int ROWS>
 struct Chunk {
-    float4 v[ROWS / 16];
+    float4 v[ROWS / (4 * NW)];
 };
 
 template <int ROWS>
@@ -129,8 +132,8 @@ __device__ __forceinline__ void load_chunk(Chunk<ROWS> &ch, const float *__restr
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int k = k0 + 4 * (lane & 7);
 #pragma unroll
-    for (int i = 0; i < ROWS / 16; ++i) {
-        const int r = 16 * i + 4 * warp + (lane >> 3);
+    for (int i = 0; i < ROWS / (4 * NW); ++i) {
+        const int r = 4 * NW * i + 4 * warp + (lane >> 3);
         ch.v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (r < rows && k < K) ch.v[i] = __ldg(reinterpret_cast<const float4 *>(src + (long long)r * ld + k));
     }
@@ -144,8 +147,8 @@ template <int ROWS>
 __device__ __forceinline__ void store_split(const Chunk<ROWS> &ch, uint32_t hi, uint32_t lo) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c = lane & 7;
 #pragma unroll
-    for (int i = 0; i < ROWS / 16; ++i) {
-        const int r = 16 * i + 4 * warp + (lane >> 3);
+    for (int i = 0; i < ROWS / (4 * NW); ++i) {
+        const int r = 4 * NW * i + 4 * warp + (lane >> 3);
         const float4 v = ch.v[i];
         const float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
         const float4 l = make_float4(tf32_rna(v.x - h.x), tf32_rna(v.y - h.y), tf32_rna(v.z - h.z), tf32_rna(v.w - h.w));
@@ -162,8 +165,8 @@ __device__ __forceinline__ void async_chunk(uint32_t dst, const float *__restric
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c = lane & 7;
     const int k = k0 + 4 * c;
 #pragma unroll
-    for (int i = 0; i < ROWS / 16; ++i) {
-        const int r = 16 * i + 4 * warp + (lane >> 3);
+    for (int i = 0; i < ROWS / (4 * NW); ++i) {
+        const int r = 4 * NW * i + 4 * warp + (lane >> 3);
         const bool in = r < rows && k < K;
         const float *g = in ? src + (long long)r * ld + k : src;
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + sw128_off(r, c)), "l"(g),
@@ -172,22 +175,23 @@ __device__ __forceinline__ void async_chunk(uint32_t dst, const float *__restric
     }
 }
 
-// C tile: thread (warp w, lane l) holds row 32w + l of the accumulator; the tile goes through shared memory (row
-// stride BN + 4 floats: the 16-byte stores of a warp fall on distinct banks) so that global stores are whole rows.
+// C tile: thread (warp w, lane l) holds row 32 (w % 4) + l of the accumulator; the tile goes through shared memory
+// (row stride BN + 4 floats: the 16-byte stores of a warp fall on distinct banks) so that global stores are whole
+// rows.
 template <int BN>
 __device__ __forceinline__ void tile_to_smem(float *tile, const float (&v)[16], int j) {
-    const int row = threadIdx.x;
+    const int row = 32 * ((threadIdx.x >> 5) & 3) + (threadIdx.x & 31);
 #pragma unroll
     for (int q = 0; q < 16; q += 4)
         *reinterpret_cast<float4 *>(tile + row * (BN + 4) + j + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
 }
 
-// Rows [0, 128) x columns [0, ncols) of the smem tile -> dst (row stride ld), warp w writing rows w, w + 4, ...
+// Rows [0, 128) x columns [0, ncols) of the smem tile -> dst (row stride ld), warp w writing rows w, w + NW, ...
 template <int BN>
 __device__ __forceinline__ void smem_to_rows(float *__restrict__ dst, long long ld, const float *tile, long long rows,
                                              int ncols) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int r = warp; r < BM && r < rows; r += 4) {
+    for (int r = warp; r < BM && r < rows; r += NW) {
         const float *src = tile + r * (BN + 4);
         float *d = dst + (long long)r * ld;
         for (int c = 4 * lane; c < ncols; c += 128) {
@@ -204,7 +208,7 @@ __device__ __forceinline__ void smem_to_rows(float *__restrict__ dst, long long 
 // [split][tile][128][BN]) and the CTA that arrives last for a tile (counter per tile, back to zero afterwards) adds
 // the partials in split order -- deterministic whichever CTA is last.
 template <int BN, int STAGES, int KS>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(NT, 1)
 k_gemm_tf32x3(const float *__restrict__ A, long long lda, const float *__restrict__ Bhi,
               const float *__restrict__ Blo, long long ldb, float *__restrict__ C, long long ldc, long long M, int N,
               int K, float *__restrict__ ws, int *__restrict__ counters) {
@@ -307,10 +311,12 @@ k_gemm_tf32x3(const float *__restrict__ A, long long lda, const float *__restric
     tc_fence_after();
     float *tile = reinterpret_cast<float *>(smem);            // the operand stages are free now
     if (ok && done) {
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        // warps w and w + 4 read the lane quadrant w % 4, each half of the columns
+        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const int npairs = nk < KS ? nk : KS;               // accumulator pairs that received MMAs
+        const int j0 = (warp >> 2) * (BN / 2);
 #pragma unroll 1
-        for (int j = 0; j < BN; j += 16) {
+        for (int j = j0; j < j0 + BN / 2; j += 16) {
             float v[16], w[16], t[16];
 #pragma unroll
             for (int q = 0; q < 16; ++q) v[q] = w[q] = 0.0f;
@@ -352,7 +358,7 @@ k_gemm_tf32x3(const float *__restrict__ A, long long lda, const float *__restric
     if (!*last_flag) return;
     __threadfence();
     // partials added in split order; each thread sums 8 float4 of the tile at a time (independent loads in flight)
-    constexpr int PER = BM * BN / 4 / 128;                    // float4 of the tile per thread
+    constexpr int PER = BM * BN / 4 / NT;                     // float4 of the tile per thread
     const float4 *part4 = reinterpret_cast<const float4 *>(ws + tile_id * BM * BN);
     const long long split_stride4 = n_tiles * BM * BN / 4;
 #pragma unroll 1
@@ -364,7 +370,7 @@ k_gemm_tf32x3(const float *__restrict__ A, long long lda, const float *__restric
         for (int z = 0; z < splits; ++z) {
             float4 t[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) t[u] = __ldcg(part4 + z * split_stride4 + tid + (b0 + u) * 128);
+            for (int u = 0; u < 8; ++u) t[u] = __ldcg(part4 + z * split_stride4 + tid + (b0 + u) * NT);
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 acc[u].x += t[u].x; acc[u].y += t[u].y; acc[u].z += t[u].z; acc[u].w += t[u].w;
@@ -372,7 +378,7 @@ k_gemm_tf32x3(const float *__restrict__ A, long long lda, const float *__restric
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-            const int q = (tid + (b0 + u) * 128) * 4, r = q / BN, c = q % BN;
+            const int q = (tid + (b0 + u) * NT) * 4, r = q / BN, c = q % BN;
             if (r >= rows_a || c >= ncols) continue;
             float *d = C + (m0 + r) * ldc + n0 + c;
             if (c + 4 <= ncols) {
