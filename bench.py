@@ -33,7 +33,8 @@ Extra keys, the other BASELINE configurations (skipped with --no-extras):
                graph, with the energy match against the same loop on the unpatched model.
 
 Profiling entry points (ncu --profile-from-start off ...): --profile step (three graph replays of the E+F step),
---profile ops [--large-cells K] (one launch of every large-system op).
+--profile ops [--large-cells K] (one launch of every large-system op), --profile gemm (the radial MLP's last-layer
+GEMM at the configs[1] layer-2 shapes).
 """
 from __future__ import annotations
 
@@ -369,6 +370,29 @@ LARGE_CELLS = 10
 TRAFFIC_FILE = os.path.join(ROOT, 'profiles', 'conv_dram_traffic.json')
 
 
+def profile_gemm(dev, M=5218):
+    """--profile gemm: the radial MLP's last layer at the configs[1] layer-2 shapes, forward W = h . Wr
+    (M x 1280 x 64) and the input gradient gh = gW . Wr^T (M x 64 x 1280), one launch each between
+    cudaProfilerStart/Stop after three warm launches."""
+    from mace_mps_kernels_b200 import gemm
+    torch.manual_seed(0)
+    cases = []
+    for m, n, k in ((M, 1280, 64), (M, 64, 1280)):
+        A, B = torch.randn(m, k, device=dev), torch.randn(n, k, device=dev)
+        hi, lo = gemm.tf32_split(B)
+        cases.append((A, hi, lo, torch.empty(m, n, device=dev)))
+    for _ in range(3):
+        for A, hi, lo, C in cases:
+            gemm.matmul_nt(A, hi, lo, out=C)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    for A, hi, lo, C in cases:
+        gemm.matmul_nt(A, hi, lo, out=C)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print(json.dumps({'profile': 'gemm', 'launch_order': [f'{m}x{n}x{k}' for m, n, k in ((M, 1280, 64), (M, 64, 1280))]}))
+
+
 def measured_traffic(kernel_pair, N, E, spec_key):
     """DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum, forward + backward launch) of this conv layer at
     exactly this graph size, from the committed ncu capture (None when no capture of this exact launch exists)."""
@@ -461,10 +485,10 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-large', action='store_true', help='skip the large-system per-op measurement')
     ap.add_argument('--large-cells', type=int, default=LARGE_CELLS, help='fcc Cu supercell edge of the large case')
-    ap.add_argument('--profile', choices=['step', 'ops'], default=None,
+    ap.add_argument('--profile', choices=['step', 'ops', 'gemm'], default=None,
                     help='run only the region to profile between cudaProfilerStart/Stop (for ncu '
-                         '--profile-from-start off): three replays of the graphed E+F step, or one launch of every '
-                         'large-system op')
+                         '--profile-from-start off): three replays of the graphed E+F step, one launch of every '
+                         'large-system op, or the radial MLP last-layer GEMM at the configs[1] layer-2 shapes')
     ap.add_argument('--partitioned', action='store_true',
                     help='only the configs[4] run: one bulk Cu system (--part-cells) partitioned by receiving atom over '
                          'the ranks (halo exchange per interaction), strong scaling')
@@ -528,6 +552,8 @@ def main():
         print(json.dumps({'profile': 'step', 'conv_launch_order': 'per replay: conv_tp[0] fwd, conv_tp[1] fwd, '
                           'conv_tp[1] bwd, conv_tp[0] bwd', 'convs': convs}))
         return
+    if a.profile == 'gemm':
+        return profile_gemm(dev)
     if a.profile == 'ops':
         cases, info = large_cases(dev, a.large_cells)
         for c in cases:                              # warm (module load, CSR) outside the profiled region

@@ -45,6 +45,9 @@
 #else
 #define MMK_BWD_BOUNDS(T) __launch_bounds__(T)
 #endif
+#ifndef MMK_WAIT_HINT_NS
+#define MMK_WAIT_HINT_NS 1000000    // ns a thread may sleep in one mbarrier.try_wait (it wakes when the phase completes)
+#endif
 #ifndef MMK_WAIT_BUDGET
 #define MMK_WAIT_BUDGET (2000000000LL)      // clock64 cycles, ~1 s (MMK_WAIT_CYCLES at layer creation overrides it)
 #endif
@@ -85,9 +88,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(u64 *bar, u32 bytes) {
 __device__ __forceinline__ bool mbar_try_wait(u64 *bar, u32 parity) {
     u32 ok;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}\n"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
+        : "r"(smem_addr(bar)), "r"(parity), "r"((unsigned)MMK_WAIT_HINT_NS)
         : "memory");
     return ok != 0;
 }
@@ -732,3 +735,286 @@ mmk_conv_bwd_kernel(const float *__restrict__ x, const float *__restrict__ Y, co
         if (part == 3) bwd_consume<STAGES, CG, CPT, NP, 3>(smem, full, empty, red_full, red_free, red, part_buf, arrived, x, Y, rowptr, gx, gY, gW, n_nodes, n_edges, nb, er, pieces, piece_flags, edone, grp, lg, u0, gwarp, lane);
     }
 }
+
+// ------------------------------------------------------------------------------------------------------------------
+// forward on the tensor cores (layers with MUL = 128; the generated header defines MMK_FWD_TC 1 and its helpers)
+// ------------------------------------------------------------------------------------------------------------------
+// Per edge e (sender s) and x block b: t[u, n] = sum_a x[s, u, a] M_b,e[a, n] with M_b,e[a, n] = sum_j c Y[e, j]
+// (the columns n of block b are its instructions' output components), then out[r, k, u, m] += W[e, k, u] t[u, n(k,m)].
+// The product runs on tcgen05 (kind::tf32, M = 128 channels in the TMEM lanes, K = 8 per block, N = the block's
+// columns padded to 16) with the 3xTF32 split (x = hi + lo and M = hi + lo; lo.hi + hi.lo + hi.hi into one fresh
+// accumulator per edge, so at most 3 MMAs add into it), the rest on the CUDA cores.  Warps of a CTA
+// (32 (4 TC_NG + 2) threads):
+//   0 .. 4 TC_NG - 1  compute: warp w serves channels u = 32 (w % 4) + lane (the TMEM lane quadrant w % 4 it may
+//        read) and column group w / 4: the 16-column TMEM groups of the layer are dealt over the TC_NG groups, and
+//        so are the output accumulators (every output component belongs to one column).  For the edge LAG ahead
+//        of its epilogue a warp stages its share of A (x[s] row of the TMA ring -> TF32 parts) and of B (entries of
+//        M_e from Y[e], spread over all compute threads); then the epilogue of the edge: its columns from tensor
+//        memory (all loads issued before one wait), W from the ring, out accumulated in registers over the
+//        receiver's edges, written once;
+//   4 TC_NG       producer: the TMA ring of (W[e], x[s], Y[e], e), as in the CUDA-core forward;
+//   4 TC_NG + 1   MMA: lane 0 issues the edge's MMAs into its TMEM slot once A and B are staged and the slot's
+//        previous epilogue is done, and commits them to t_full.
+// Edge slots (A, B, 128 TMEM columns) form a ring of NS.  A compute warp restages slot (q mod NS) only after its own
+// wait for the MMAs of edge q - NS (its epilogue of that edge), so the operands are free when it writes them.  Every
+// wait is bounded and every role reaches the teardown (tensor memory freed) also on the error path.
+#if MMK_FWD_TC
+__device__ __forceinline__ float tc_rna(float v) {
+    u32 r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+    return __uint_as_float(r);
+}
+__device__ __forceinline__ void tc_st4(u32 addr, float a, float b, float c, float d) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+// 16-byte piece c (K = 4c .. 4c+3) of A row u, split into the high and low TF32 tiles (128-byte swizzle)
+__device__ __forceinline__ void tc_put_a(u32 a_hi, u32 a_lo, int u, int c, const float (&v)[4]) {
+    const u32 off = (u32)u * 128u + ((u32)(c ^ (u & 7)) << 4);
+    float h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        h[i] = tc_rna(v[i]);
+        l[i] = tc_rna(v[i] - h[i]);
+    }
+    tc_st4(a_hi + off, h[0], h[1], h[2], h[3]);
+    tc_st4(a_lo + off, l[0], l[1], l[2], l[3]);
+}
+// 16 consecutive TMEM columns of this thread's lane; the values are valid after tc_wait_ld()
+__device__ __forceinline__ void tc_ld16(u32 taddr, u32 (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ unsigned long long tc_desc(u32 saddr) {      // K-major, 128-byte swizzle, 8-row groups 1 KB apart
+    return (unsigned long long)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((unsigned long long)(1024 >> 4) << 32) |
+           (1ull << 46) | (2ull << 61);
+}
+__device__ __forceinline__ void tc_mma(u32 d, unsigned long long a, unsigned long long b, u32 idesc, u32 acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(u64 *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// the CTA's edges in order: node chunks dealt round-robin (nb nodes each), nodes in order, CSR edges in order
+struct TcCursor {
+    long long chunk, n, n1;
+    int p, p1;
+    bool live;
+};
+__device__ __forceinline__ void tc_open(TcCursor &c, const int *rowptr, long long nb, long long n_nodes) {
+    c.chunk = blockIdx.x;
+    c.live = false;
+    for (; c.chunk * nb < n_nodes; c.chunk += gridDim.x) {
+        for (c.n = c.chunk * nb, c.n1 = min(n_nodes, c.chunk * nb + nb); c.n < c.n1; ++c.n) {
+            c.p = rowptr[c.n];
+            c.p1 = rowptr[c.n + 1];
+            if (c.p < c.p1) {
+                c.live = true;
+                return;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void tc_next(TcCursor &c, const int *rowptr, long long nb, long long n_nodes) {
+    if (++c.p < c.p1) return;
+    for (++c.n;; ++c.n) {
+        if (c.n >= c.n1) {
+            c.chunk += gridDim.x;
+            if (c.chunk * nb >= n_nodes) {
+                c.live = false;
+                return;
+            }
+            c.n = c.chunk * nb;
+            c.n1 = min(n_nodes, c.n + nb);
+        }
+        c.p = rowptr[c.n];
+        c.p1 = rowptr[c.n + 1];
+        if (c.p < c.p1) return;
+    }
+}
+
+template <int STAGES, int NS>
+__global__ void __launch_bounds__(32 * (4 * TC_NG + 2), 1)
+mmk_conv_fwd_tc_kernel(const float *__restrict__ x, const float *__restrict__ Y, const float *__restrict__ W,
+                       const int *__restrict__ rowptr, const int *__restrict__ eids,
+                       const long long *__restrict__ senders, float *__restrict__ out, long long n_nodes,
+                       long long n_edges, long long nb) {
+    constexpr int NCW = 4 * TC_NG;                    // compute warps
+    constexpr int LAG = NS - 1;                       // edges staged ahead of the epilogue
+    constexpr u32 STAGE_F = W_DIM + X_DIM + 20;       // W row | x row | Y row (16) | edge id (4)
+    constexpr u32 A_BYTES = 128 * 128, B_BYTES = TC_BROWS * 128, SLOT = 2 * A_BYTES + 2 * B_BYTES;
+    static_assert(MUL == 128 && YD == 16, "tensor-core forward: 128 channels, Y rows of 16");
+    static_assert(STAGES > LAG, "the ring must hold the staged edges");
+    extern __shared__ __align__(1024) float smem_tc[];
+    unsigned char *base = reinterpret_cast<unsigned char *>((reinterpret_cast<unsigned long long>(smem_tc) + 1023) & ~1023ull);
+    const u32 slots = smem_addr(base);
+    float *ring = reinterpret_cast<float *>(base + NS * SLOT);
+    u64 *full = reinterpret_cast<u64 *>(ring + STAGES * STAGE_F);
+    u64 *empty = full + STAGES;
+    u64 *ab_full = empty + STAGES;                    // [NS] the compute warps staged A and B
+    u64 *t_full = ab_full + NS;                       // [NS] the edge's MMAs completed
+    u64 *t_free = t_full + NS;                        // [NS] the edge's epilogue read its TMEM slot
+    u32 *tmem_box = reinterpret_cast<u32 *>(t_free + NS);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NCW);
+        }
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&ab_full[s], NCW);
+            mbar_init(&t_full[s], 1);
+            mbar_init(&t_free[s], NCW);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // the B tiles are written only at their structurally nonzero entries: everything else must read as zero
+    for (u32 i = tid; i < NS * 2 * B_BYTES / 16; i += blockDim.x) {
+        const u32 sl = i / (2 * B_BYTES / 16), o = (i % (2 * B_BYTES / 16)) * 16;
+        tc_st4(slots + sl * SLOT + 2 * A_BYTES + o, 0.f, 0.f, 0.f, 0.f);
+    }
+    release_fence();
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_addr(tmem_box))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const u32 tmem = *tmem_box;
+    const ERange er{0, n_edges, 0, n_nodes};
+
+    if (warp == NCW) {                                 // producer
+#ifndef MMK_TEST_STALL
+        u32 it = 0;
+        auto issue = [&](u32 st, long long e, long long s, u64 *bar) {
+            float *stage = ring + st * STAGE_F;
+            *reinterpret_cast<long long *>(stage + W_DIM + X_DIM + 16) = e;
+            mbar_arrive_expect_tx(bar, (W_DIM + X_DIM + YD) * 4);
+            bulk_g2s(stage, W + e * W_DIM, W_DIM * 4, bar);
+            bulk_g2s(stage + W_DIM, x + s * X_DIM, X_DIM * 4, bar);
+            bulk_g2s(stage + W_DIM + X_DIM, Y + e * YD, YD * 4, bar);
+        };
+        long long chunk = blockIdx.x, n0, n1;
+        while (next_chunk(chunk, nb, n_nodes, er, n0, n1)) {
+            if (!produce<STAGES>(rowptr, eids, senders, n0, n1, er, n_nodes, n_edges, full, empty, it, issue)) {
+                if (lane == 0) atomicExch(&mmk_status, 1);
+                break;
+            }
+        }
+#endif
+    } else if (warp == NCW + 1) {                      // MMA issue
+        TcCursor c;
+        tc_open(c, rowptr, nb, n_nodes);
+        bool ok = true;
+        long long issued = -1;                         // last edge whose MMAs were committed
+        for (u32 q = 0; c.live && ok; ++q, tc_next(c, rowptr, nb, n_nodes)) {
+            const u32 sl = q % NS;
+            ok = __all_sync(0xffffffffu,
+                            mbar_wait(&ab_full[sl], (q / NS) & 1) && mbar_wait(&t_free[sl], ((q / NS) & 1) ^ 1));
+            if (!ok) break;
+            if (lane == 0) {
+                tc_fence_after();
+                const u32 a_hi = slots + sl * SLOT, a_lo = a_hi + A_BYTES, b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + B_BYTES;
+#pragma unroll
+                for (int b = 0; b < TC_NB; ++b) {
+                    const u32 d = tmem + sl * 128 + tc_col0(b);
+                    const u32 idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((u32)(tc_ncol(b) >> 3) << 17) | ((128u >> 4) << 24);
+                    const u32 ko = 32u * b;
+                    tc_mma(d, tc_desc(a_lo + ko), tc_desc(b_hi + ko), idesc, 0u);
+                    tc_mma(d, tc_desc(a_hi + ko), tc_desc(b_lo + ko), idesc, 1u);
+                    tc_mma(d, tc_desc(a_hi + ko), tc_desc(b_hi + ko), idesc, 1u);
+                }
+                tc_commit(&t_full[sl]);
+            }
+            issued = q;
+            __syncwarp();
+        }
+        if (!ok && lane == 0) atomicExch(&mmk_status, 12);
+        // the tensor memory is freed at the end: wait (bounded) for the last committed MMAs
+        if (issued >= 0) mbar_wait(&t_full[issued % NS], (u32)(issued / NS) & 1);
+    } else if (warp < NCW) {                           // compute: channel u, column group g
+        const int g = warp >> 2, u = ((warp & 3) << 5) | lane;
+        const u32 tlane = (u32)((warp & 3) * 32) << 16;
+        TcCursor cs;                                   // staging cursor, LAG edges ahead of the epilogue
+        tc_open(cs, rowptr, nb, n_nodes);
+        bool ok = true;
+        u32 qs = 0, qe = 0;
+        float acc[TC_ACC];
+#pragma unroll
+        for (int i = 0; i < TC_ACC; ++i) acc[i] = 0.0f;
+        // nodes in order; edgeless nodes are written as zeros
+        long long chunk = blockIdx.x, n0, n1;
+        while (ok && next_chunk(chunk, nb, n_nodes, er, n0, n1))
+            for (long long n = n0; n < n1 && ok; ++n) {
+                for (int p = rowptr[n]; p < rowptr[n + 1] && ok; ++p, ++qe) {
+                    while (cs.live && qs <= qe + LAG) {  // stage A and B of edge qs
+                        const u32 st = qs % STAGES, sl = qs % NS;
+                        if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (qs / STAGES) & 1))) {
+                            ok = false;
+                            break;
+                        }
+                        const float *stage = ring + st * STAGE_F;
+                        const u32 a_hi = slots + sl * SLOT, a_lo = a_hi + A_BYTES;
+                        const u32 b_hi = a_hi + 2 * A_BYTES, b_lo = b_hi + B_BYTES;
+                        tc_stage_a(g, stage + W_DIM, u, a_hi, a_lo);
+                        const float *ys = stage + W_DIM + X_DIM;
+                        for (int i = tid; i < TC_NE; i += 32 * NCW) {
+                            float v = 0.0f;
+#pragma unroll
+                            for (int j = 0; j < TC_EMAX; ++j) v = fmaf(tc_e_c[i * TC_EMAX + j], ys[tc_e_y[i * TC_EMAX + j]], v);
+                            const float hv = tc_rna(v), lv = tc_rna(v - hv);
+                            const u32 o = tc_e_off[i];
+                            asm volatile("st.shared.f32 [%0], %1;" ::"r"(b_hi + o), "f"(hv) : "memory");
+                            asm volatile("st.shared.f32 [%0], %1;" ::"r"(b_lo + o), "f"(lv) : "memory");
+                        }
+                        release_fence();               // A and B written (generic) -> read by the MMA (async proxy)
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&ab_full[sl]);
+                        ++qs;
+                        tc_next(cs, rowptr, nb, n_nodes);
+                    }
+                    if (!ok) break;
+                    const u32 st = qe % STAGES, sl = qe % NS;
+                    if (!__all_sync(0xffffffffu, mbar_wait(&t_full[sl], (qe / NS) & 1))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    tc_epilogue(g, ring + st * STAGE_F, u, tmem + tlane + sl * 128, acc);
+                    tc_fence_before();
+                    release_fence();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&t_free[sl]);
+                        mbar_arrive(&empty[st]);
+                    }
+                }
+                if (!ok) break;
+                tc_store(g, out + n * OUT_DIM, u, acc);
+#pragma unroll
+                for (int i = 0; i < TC_ACC; ++i) acc[i] = 0.0f;
+            }
+        if (!ok && lane == 0) atomicExch(&mmk_status, 13);
+    }
+    // teardown: wait (bounded) until the last MMAs completed, then free the tensor memory
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    }
+}
+#endif

@@ -39,6 +39,8 @@ constexpr int NW = 8;                   // warps per CTA (two per tensor-memory 
 constexpr int NT = 32 * NW;             // threads per CTA
 constexpr int BK = 32;                  // K chunk: 32 floats = one 128-byte swizzle row
 constexpr long long WAIT_BUDGET = 2000000000LL;   // clock64 cycles (~1 s)
+// a waiting thread sleeps in mbarrier.try_wait until the phase completes or this many ns pass, instead of spinning
+constexpr unsigned WAIT_HINT_NS = 1000000;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -55,9 +57,9 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}\n"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"((unsigned)WAIT_HINT_NS)
         : "memory");
     return ok != 0;
 }

@@ -19,6 +19,9 @@
 // T[e, c, row_t + m] g[b, off + c*M + m]) d(x^idx_t)/dx_i.  Waits are bounded as in conv_tp.cuh.
 #include "mmk_layer.h"
 
+#ifndef MMK_WAIT_HINT_NS
+#define MMK_WAIT_HINT_NS 1000000    // ns a thread may sleep in one mbarrier.try_wait (it wakes when the phase completes)
+#endif
 #ifndef MMK_WAIT_BUDGET
 #define MMK_WAIT_BUDGET (2000000000LL)              // clock64 cycles, ~1 s (MMK_WAIT_CYCLES overrides it)
 #endif
@@ -52,9 +55,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(u64 *bar, u32 bytes) {
 __device__ __forceinline__ bool mbar_try_wait(u64 *bar, u32 parity) {
     u32 ok;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}\n"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
+        : "r"(smem_addr(bar)), "r"(parity), "r"((unsigned)MMK_WAIT_HINT_NS)
         : "memory");
     return ok != 0;
 }

@@ -54,6 +54,18 @@ def test_generated_conv_source_compiles(hidden, lmax):
     _lib.check(_lib.lib().mmk_conv_compile_check(ctypes.byref(d)))
 
 
+@pytest.mark.parametrize('hidden', ['128x0e', '128x0e+128x1o', '128x0e+128x1o+128x2e'])
+@pytest.mark.parametrize('groups', ['1', '4'])
+def test_generated_tensor_core_forward_compiles(monkeypatch, hidden, groups):
+    """The tcgen05 forward variant (MMK_CONV_FWD_TC=1, 128-channel layers) with one and with four column groups."""
+    from mace_mps_kernels_b200 import _lib
+    from mace_mps_kernels_b200.conv import ConvSpec
+    monkeypatch.setenv('MMK_CONV_FWD_TC', '1')
+    monkeypatch.setenv('MMK_CONV_TC_GROUPS', groups)
+    d = ConvSpec(helpers.conv_tp(hidden, 3)).descriptor()
+    _lib.check(_lib.lib().mmk_conv_compile_check(ctypes.byref(d)))
+
+
 def test_generated_sc_source_compiles():
     from mace_mps_kernels_b200 import _lib
     from mace_mps_kernels_b200.symmetric import SCSpec

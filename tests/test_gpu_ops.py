@@ -52,6 +52,7 @@ def test_conv_fwd_bwd_matches_oracle(cuda, hidden, lmax, N, E):
 PLAN_VARIANTS = [
     {'MMK_CONV_EDGE_SPLIT': '0'},              # node ranges per CTA on small graphs (no pieces)
     {'MMK_CONV_EDGE_SPLIT': '1'},              # edge-balanced ranges in both directions (default: backward only)
+    {'MMK_CONV_FWD_TC': '1'},                  # forward on the tensor cores (layers with 128 channels)
     {'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2'},
     {'MMK_CONV_FWD_CPT': '4', 'MMK_CONV_BWD_CPT': '4', 'MMK_CONV_FWD_CG': '8', 'MMK_CONV_BWD_CG': '8'},
     {'MMK_CONV_FWD_CPT': '2', 'MMK_CONV_BWD_CPT': '2', 'MMK_CONV_FWD_CG': '8', 'MMK_CONV_BWD_CG': '8'},
@@ -246,3 +247,11 @@ def test_conv_edge_split_repeatable_and_equal_to_node_ranges(cuda, monkeypatch, 
     nodes = run(CudaConvTP(tp))
     for a, b, name in zip(first, nodes, ('out', 'gx', 'gY', 'gW')):
         close(a, b.double().cpu().numpy(), what=name)
+
+
+@pytest.mark.parametrize('hidden,lmax,N,E', [c for c in CONV_CASES if c[0].startswith('128x')])
+def test_conv_tensor_core_forward_matches_oracle(cuda, monkeypatch, hidden, lmax, N, E):
+    """The tcgen05 forward (per-edge x . M_e with the 3xTF32 split, W weighting and receiver sums on the CUDA cores)
+    against the float64 oracle, on every 128-channel case; the backward is the CUDA-core kernel."""
+    monkeypatch.setenv('MMK_CONV_FWD_TC', '1')
+    _conv_case(cuda, hidden, lmax, N, E)
