@@ -222,6 +222,28 @@ MMK_API int mmk_radial_fwd(const mmk_radial_desc *desc, const float *lengths, in
 MMK_API int mmk_radial_bwd(const mmk_radial_desc *desc, const float *lengths, const float *grad_out, int64_t n_edges,
                            float *grad_lengths, void *stream);
 
+/* MACE's get_edge_vectors_and_lengths (mace/modules/utils.py): vectors[e] = positions[edge_index[1, e]] -
+ * positions[edge_index[0, e]] + shifts[e] (float32, PyTorch's order of operations) and lengths[e] = |vectors[e]|.
+ *   positions [n_nodes, 3], shifts [E, 3], vectors [E, 3], lengths [E] (device float32); edge_index device int64
+ *   [2, E] (row 0 senders, row 1 receivers). */
+MMK_API int mmk_edge_vectors_fwd(const float *positions, const int64_t *edge_index, const float *shifts,
+                                 int64_t n_edges, float *vectors, float *lengths, void *stream);
+/* Backward: g[e] = grad_vectors[e] + vectors[e] * (grad_lengths[e] / lengths[e]) (the length term is 0 where the
+ * length is 0, as PyTorch's norm backward; either incoming gradient may be NULL, not both);
+ * grad_positions[n] = sum of g over n's receiver CSR row - sum of g over n's sender CSR row (CSRs as mmk_csr_build
+ * makes them; one warp per node, fixed summation order: deterministic); grad_shifts[e] = g[e].  grad_positions or
+ * grad_shifts may be NULL (not computed). */
+MMK_API int mmk_edge_vectors_bwd(const float *grad_vectors, const float *grad_lengths, const float *vectors,
+                                 const float *lengths, const int32_t *recv_rowptr, const int32_t *recv_eids,
+                                 const int32_t *send_rowptr, const int32_t *send_eids, int64_t n_nodes,
+                                 int64_t n_edges, float *grad_positions, float *grad_shifts, void *stream);
+
+/* out[r, j] = x[r, cols[j]] for r < n_rows, j < n_cols (device float32, row-major with leading dimensions ldx, ldo;
+ * cols device int32).  With cols a permutation it is MACE's reshape_irreps ([N, sum mul (2l+1)] in irreps layout ->
+ * [N, mul, sum (2l+1)]) and, with the inverse permutation, its backward. */
+MMK_API int mmk_gather_columns(const float *x, int64_t ldx, float *out, int64_t ldo, const int32_t *cols,
+                               int64_t n_rows, int n_cols, void *stream);
+
 /* ------------------------------------------------------------------------------------------------------------------
  * neighbour list (no counterpart in the reference, which takes the graph MACE builds on the host): the periodic pairs
  * within the cutoff, built on the device

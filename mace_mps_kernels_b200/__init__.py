@@ -21,7 +21,8 @@ import torch
 
 from .conv import CudaConvTP, MetalConvTP, conv_supported
 from .dense import CudaLinear, CudaSkipTP
-from .edge import CudaRadialEmbedding, CudaSphericalHarmonics, radial_supported, sh_supported
+from .edge import (CudaRadialEmbedding, CudaSphericalHarmonics, patch_edge_vectors, radial_supported,
+                   sh_supported)
 from .symmetric import CudaSymmetricContraction, MetalSymmetricContraction, sc_supported
 
 __version__ = '0.1.0'
@@ -43,8 +44,10 @@ def patch_model(model, conv=True, symmetric=True, verbose=True, edge_features=Fa
     expose MACE's ``conv_fusion`` path, product blocks without the cuequivariance layout; already-patched blocks are
     left alone (idempotent) and every skip is reported (and warned about when ``verbose``).  Extensions beyond the
     reference, off by default so that the default report is the reference's: ``edge_features=True`` also swaps
-    ``spherical_harmonics`` and ``radial_embedding``; ``linears=True`` swaps every equivariant linear layer and the
-    element-indexed skip connections (frozen weights only, see ``dense.py``)."""
+    ``spherical_harmonics`` and ``radial_embedding`` and routes the model's ``get_edge_vectors_and_lengths`` to one
+    fused launch each way (see ``edge.patch_edge_vectors``); ``linears=True`` swaps every equivariant linear layer,
+    the element-indexed skip connections, the radial MLPs and the interactions' ``reshape`` (frozen weights only,
+    see ``dense.py``)."""
     p0 = next(model.parameters())
     dev = p0.device
     if dev.type != 'cuda':
@@ -99,9 +102,12 @@ def patch_model(model, conv=True, symmetric=True, verbose=True, edge_features=Fa
                     continue
                 setattr(model, name, cls(mod))
                 patched.append(name)
+            ok, why = patch_edge_vectors(model)
+            (patched.append('get_edge_vectors_and_lengths') if ok
+             else skipped.append(('get_edge_vectors_and_lengths', why)))
         if linears:
-            from .dense import (CudaFullyConnectedNet, CudaLinear, CudaSkipTP, linear_supported, mlp_supported,
-                                skip_supported)
+            from .dense import (CudaFullyConnectedNet, CudaLinear, CudaReshapeIrreps, CudaSkipTP, linear_supported,
+                                mlp_supported, reshape_supported, skip_supported)
             for pname, parent in list(model.named_modules()):
                 for cname, child in list(parent.named_children()):
                     kind = type(child).__name__
@@ -111,6 +117,8 @@ def patch_model(model, conv=True, symmetric=True, verbose=True, edge_features=Fa
                         cls, (ok, why) = CudaSkipTP, skip_supported(child)
                     elif kind == 'FullyConnectedNet' and hasattr(child, 'hs'):
                         cls, (ok, why) = CudaFullyConnectedNet, mlp_supported(child)
+                    elif kind == 'reshape_irreps':
+                        cls, (ok, why) = (lambda c: CudaReshapeIrreps(c, device=dev)), reshape_supported(child)
                     else:
                         continue
                     full = f'{pname}.{cname}' if pname else cname

@@ -60,6 +60,9 @@ SIGNATURES = {
     'mmk_sh_bwd': (_i, [_p, _p, _i64, _i, _p, _p]),
     'mmk_radial_fwd': (_i, [ctypes.POINTER(RadialDesc), _p, _i64, _p, _p]),
     'mmk_radial_bwd': (_i, [ctypes.POINTER(RadialDesc), _p, _p, _i64, _p, _p]),
+    'mmk_edge_vectors_fwd': (_i, [_p, _p, _p, _i64, _p, _p, _p]),
+    'mmk_edge_vectors_bwd': (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p]),
+    'mmk_gather_columns': (_i, [_p, _i64, _p, _i64, _p, _i64, _i, _p]),
     'mmk_block_linear': (_i, [_p, _i64, _p, _i64, _p, _i, _p, _p, _i, _i, _p, _p, _i, _i64, _p]),
     'mmk_block_linear_act': (_i, [_p, _i64, _p, _i64, _p, _i, _p, _p, _i, _i, _p, _p, _i, _i64, _i, _p, _i, _p,
                                   ctypes.c_float, _p]),
@@ -113,7 +116,8 @@ KERNELS_PER_CALL = {'mmk_conv_fwd': 1, 'mmk_conv_bwd': 1, 'mmk_sc_fwd': 1, 'mmk_
                     'mmk_csr_build_noalloc': 4, 'mmk_elem_index': 1, 'mmk_elem_groups': 3,
                     'mmk_sh_fwd': 1, 'mmk_sh_bwd': 1, 'mmk_radial_fwd': 1, 'mmk_radial_bwd': 1,
                     'mmk_block_linear': 1, 'mmk_block_linear_act': 1, 'mmk_mlp_fwd': 1, 'mmk_mlp_bwd': 1,
-                    'mmk_neighbor_list': 10, 'mmk_tf32_split': 1, 'mmk_gemm_tf32x3': 1}
+                    'mmk_neighbor_list': 10, 'mmk_tf32_split': 1, 'mmk_gemm_tf32x3': 1,
+                    'mmk_edge_vectors_fwd': 1, 'mmk_edge_vectors_bwd': 1, 'mmk_gather_columns': 1}
 LAUNCHES = collections.Counter()
 
 

@@ -287,3 +287,69 @@ class CudaFullyConnectedNet(torch.nn.Module):
         else:
             h = _MLPHiddenFn.apply(x, self)
         return self.last(h)
+
+
+def reshape_supported(mod):
+    """(ok, reason) for MACE's ``reshape_irreps`` module (irreps layout -> [N, mul, sum (2l+1)])."""
+    irreps = getattr(mod, 'irreps', None)
+    if irreps is None or not hasattr(mod, 'muls') or not hasattr(mod, 'dims'):
+        return False, 'not a reshape_irreps module'
+    if getattr(mod, 'cueq_config', None) is not None and getattr(mod.cueq_config, 'enabled', False):
+        return False, 'cuequivariance layout'
+    if len(set(int(m) for m in mod.muls)) != 1:
+        return False, 'unequal multiplicities'
+    return True, ''
+
+
+class _GatherColumnsFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, fwd, bwd, shape):
+        xc = x.contiguous()
+        if xc.dtype != torch.float32 or not xc.is_cuda:
+            raise TypeError('input must be a float32 CUDA tensor')
+        N, D = xc.shape
+        out = torch.empty((N,) + tuple(shape), device=xc.device, dtype=torch.float32)
+        _lib.call('mmk_gather_columns', _lib.ptr(xc), D, _lib.ptr(out), D, _lib.ptr(fwd), N, D, _lib.stream_of(xc))
+        ctx.bwd = bwd
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        if torch.is_grad_enabled():
+            raise RuntimeError(DOUBLE_BACKWARD_MSG)
+        gc = g.contiguous()
+        N = gc.shape[0]
+        D = gc.numel() // max(N, 1)
+        gx = torch.empty(N, D, device=gc.device, dtype=torch.float32)
+        _lib.call('mmk_gather_columns', _lib.ptr(gc), D, _lib.ptr(gx), D, _lib.ptr(ctx.bwd), N, D, _lib.stream_of(gc))
+        return gx, None, None, None
+
+
+class CudaReshapeIrreps(torch.nn.Module):
+    """Drop-in for MACE's ``reshape_irreps``: [N, sum mul (2l+1)] (mul_ir layout) -> [N, mul, sum (2l+1)], one
+    column-gather launch each way (C ABI ``mmk_gather_columns``) instead of a slice + reshape + cat forward and a
+    zero-fill + copy + add per block backward."""
+
+    def __init__(self, mod, device=None):
+        super().__init__()
+        ok, why = reshape_supported(mod)
+        if not ok:
+            raise ValueError(why)
+        self.irreps = mod.irreps
+        self.muls, self.dims = list(mod.muls), list(mod.dims)
+        mul, dsum = int(self.muls[0]), int(sum(self.dims))
+        fwd = np.empty((mul, dsum), dtype=np.int32)          # out[n, u, off_b + m] = x[n, xoff_b + u d_b + m]
+        xoff = off = 0
+        for d in self.dims:
+            fwd[:, off:off + d] = xoff + np.arange(mul)[:, None] * d + np.arange(d)[None, :]
+            xoff += mul * d
+            off += d
+        fwd = fwd.reshape(-1)
+        bwd = np.empty_like(fwd)
+        bwd[fwd] = np.arange(fwd.size, dtype=np.int32)
+        self.register_buffer('fwd_cols', torch.from_numpy(fwd).to(device), persistent=False)
+        self.register_buffer('bwd_cols', torch.from_numpy(bwd).to(device), persistent=False)
+        self.shape = (mul, dsum)
+
+    def forward(self, tensor):
+        return _GatherColumnsFn.apply(tensor, self.fwd_cols, self.bwd_cols, self.shape)

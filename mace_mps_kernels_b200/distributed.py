@@ -25,7 +25,7 @@ import numpy as np
 import torch
 
 from .standin.graph import neighbor_list
-from .standin.modules import RealAgnosticInteractionBlock, reshape_irreps, scatter_sum
+from .standin.modules import RealAgnosticInteractionBlock, scatter_sum
 from .standin.structures import morton_order
 
 
@@ -215,7 +215,7 @@ class DistributedMACE:
                 sc = None
             else:
                 sc = inter.skip_tp(node_feats[:n_own], attrs_own)
-            node_feats_own = prod(reshape_irreps(msg, inter.irreps_out), sc, attrs_own)
+            node_feats_own = prod(inter.reshape(msg), sc, attrs_own)
             node_es = node_es + readout(node_feats_own).squeeze(-1)
         node_energy = attrs_own @ m.atomic_energies.to(attrs_own.dtype) + m.scale * node_es + m.shift
         energy = node_energy.sum()

@@ -145,3 +145,100 @@ class CudaRadialEmbedding(torch.nn.Module):
 
     def forward(self, edge_lengths):
         return _RadialFn.apply(edge_lengths, self)
+
+
+class _EdgeVectorsFn(torch.autograd.Function):
+    """(vectors [E, 3], lengths [E, 1]) of MACE's ``get_edge_vectors_and_lengths`` in one launch; the backward is
+    one launch over the receiver and sender CSRs (built once per edge_index and shared with the convolution),
+    deterministic, where PyTorch's indexing backward sorts the edge index every call."""
+
+    @staticmethod
+    def forward(ctx, positions, shifts, edge_index):
+        from .conv import graph_csr
+        pos, sh = positions.contiguous(), shifts.contiguous()
+        for name, t in (('positions', pos), ('shifts', sh)):
+            if t.dtype != torch.float32 or not t.is_cuda:
+                raise TypeError(f'{name} must be a float32 CUDA tensor')
+        E = edge_index.shape[1]
+        vec = torch.empty(E, 3, device=pos.device, dtype=torch.float32)
+        ln = torch.empty(E, 1, device=pos.device, dtype=torch.float32)
+        _lib.call('mmk_edge_vectors_fwd', _lib.ptr(pos), _lib.ptr(edge_index), _lib.ptr(sh), E, _lib.ptr(vec),
+                  _lib.ptr(ln), _lib.stream_of(pos))
+        ctx.csr = graph_csr(edge_index, pos.shape[0]) if ctx.needs_input_grad[0] else None
+        ctx.n_nodes = pos.shape[0]
+        ctx.save_for_backward(vec, ln)
+        return vec, ln
+
+    @staticmethod
+    def backward(ctx, gvec, glen):
+        if torch.is_grad_enabled():
+            raise RuntimeError(DOUBLE_BACKWARD_MSG)
+        vec, ln = ctx.saved_tensors
+        E, N = vec.shape[0], ctx.n_nodes
+        if gvec is None and glen is None:
+            return None, None, None
+        gvec = gvec.contiguous() if gvec is not None else None
+        glen = glen.contiguous() if glen is not None else None
+        gpos = gsh = None
+        if ctx.needs_input_grad[0]:
+            gpos = torch.empty(N, 3, device=vec.device, dtype=torch.float32)
+        if ctx.needs_input_grad[1]:
+            gsh = torch.empty(E, 3, device=vec.device, dtype=torch.float32)
+        rrp, reid, srp, seid = ctx.csr if ctx.csr is not None else (None,) * 4
+        _lib.call('mmk_edge_vectors_bwd', _lib.ptr(gvec) if gvec is not None else None,
+                  _lib.ptr(glen) if glen is not None else None, _lib.ptr(vec), _lib.ptr(ln),
+                  _lib.ptr(rrp) if rrp is not None else None, _lib.ptr(reid) if reid is not None else None,
+                  _lib.ptr(srp) if srp is not None else None, _lib.ptr(seid) if seid is not None else None,
+                  N, E, _lib.ptr(gpos) if gpos is not None else None, _lib.ptr(gsh) if gsh is not None else None,
+                  _lib.stream_of(vec))
+        return gpos, gsh, None
+
+
+def edge_vectors_and_lengths(positions, edge_index, shifts):
+    """CUDA drop-in for MACE's ``get_edge_vectors_and_lengths(positions, edge_index, shifts)`` (normalize=False):
+    float32 CUDA positions and shifts, a contiguous int64 [2, E] edge_index."""
+    return _EdgeVectorsFn.apply(positions, shifts, edge_index)
+
+
+_ACTIVE = [0]            # patched models whose forward is running (the wrapper is global to the model's module)
+
+
+def _fused_get_edge_vectors_and_lengths(original):
+    def get_edge_vectors_and_lengths(positions, edge_index, shifts, normalize=False, eps=1e-9):
+        if (_ACTIVE[0] > 0 and not normalize and positions.is_cuda and positions.dtype == torch.float32
+                and shifts.dtype == torch.float32 and edge_index.dtype == torch.int64 and edge_index.dim() == 2
+                and edge_index.is_contiguous() and shifts.shape == (edge_index.shape[1], 3)):
+            return edge_vectors_and_lengths(positions, edge_index, shifts)
+        return original(positions=positions, edge_index=edge_index, shifts=shifts, normalize=normalize, eps=eps)
+
+    get_edge_vectors_and_lengths._mmk_original = original
+    return get_edge_vectors_and_lengths
+
+
+def _enter(module, args, kwargs=None):
+    _ACTIVE[0] += 1
+
+
+def _leave(module, args, output):
+    _ACTIVE[0] = max(0, _ACTIVE[0] - 1)
+
+
+def patch_edge_vectors(model):
+    """(ok, reason): route the model's ``get_edge_vectors_and_lengths`` calls to the fused CUDA op.
+
+    MACE's forward calls the function through its module's namespace (mace.modules.models imports it from
+    mace.modules.utils), so that name is replaced by a wrapper; the wrapper takes the CUDA path only while the
+    forward of a model patched here is running (forward pre/post hooks on the model) and for the supported inputs,
+    and calls the original function otherwise, so other models of the same class are unaffected."""
+    import sys
+    mod = sys.modules.get(type(model).__module__)
+    fn = getattr(mod, 'get_edge_vectors_and_lengths', None) if mod is not None else None
+    if not callable(fn):
+        return False, 'the model forward does not call get_edge_vectors_and_lengths from its module'
+    if not hasattr(fn, '_mmk_original'):
+        setattr(mod, 'get_edge_vectors_and_lengths', _fused_get_edge_vectors_and_lengths(fn))
+    if not getattr(model, '_mmk_edge_vectors', False):
+        model.register_forward_pre_hook(_enter)
+        model.register_forward_hook(_leave)
+        model._mmk_edge_vectors = True
+    return True, ''

@@ -80,13 +80,34 @@ class FullyConnectedNet(torch.nn.Module):
         return x
 
 
-def reshape_irreps(x, irreps):
-    """[N, sum mul*(2l+1)] in mul_ir layout -> [N, C, sum (2l+1)] (channel-major), equal multiplicities."""
-    N = x.shape[0]
-    parts = []
-    for sl, (mul, ir) in zip(irreps.slices(), irreps):
-        parts.append(x[:, sl].reshape(N, mul, ir.dim))
-    return torch.cat(parts, dim=-1)
+class reshape_irreps(torch.nn.Module):
+    """[N, sum mul*(2l+1)] in mul_ir layout -> [N, C, sum (2l+1)] (channel-major), equal multiplicities; mace-torch's
+    ``reshape_irreps`` module (mace/modules/irreps_tools.py), held by every interaction block as ``reshape``."""
+
+    def __init__(self, irreps):
+        super().__init__()
+        self.irreps = o3.Irreps(irreps)
+        self.dims = [ir.dim for _, ir in self.irreps]
+        self.muls = [mul for mul, _ in self.irreps]
+
+    def forward(self, tensor):
+        N = tensor.shape[0]
+        parts, ix = [], 0
+        for mul, d in zip(self.muls, self.dims):
+            parts.append(tensor[:, ix:ix + mul * d].reshape(N, mul, d))
+            ix += mul * d
+        return torch.cat(parts, dim=-1)
+
+
+def get_edge_vectors_and_lengths(positions, edge_index, shifts, normalize=False, eps=1e-9):
+    """mace-torch's edge geometry (mace/modules/utils.py): vectors receiver - sender + shift and their lengths,
+    called from the model's forward through this module's namespace."""
+    sender, receiver = edge_index[0], edge_index[1]
+    vectors = positions[receiver] - positions[sender] + shifts
+    lengths = torch.linalg.norm(vectors, dim=-1, keepdim=True)
+    if normalize:
+        return vectors / (lengths + eps), lengths
+    return vectors, lengths
 
 
 class _InteractionBase(torch.nn.Module):
@@ -109,6 +130,7 @@ class _InteractionBase(torch.nn.Module):
                                                  + [self.conv_tp.weight_numel])
         self.irreps_out = self.target_irreps
         self.linear = o3.Linear(irreps_mid, self.irreps_out)
+        self.reshape = reshape_irreps(self.irreps_out)
 
     def _conv(self, node_feats, edge_attrs, tp_weights, edge_index):
         raise NotImplementedError
@@ -133,7 +155,7 @@ class RealAgnosticInteractionBlock(_InteractionBase):
             message = scatter_sum(mji, receiver, num_nodes)
         message = self.linear(message) / self.avg_num_neighbors
         message = self.skip_tp(message, node_attrs)
-        return reshape_irreps(message, self.irreps_out), None
+        return self.reshape(message), None
 
 
 class RealAgnosticResidualInteractionBlock(_InteractionBase):
@@ -156,7 +178,7 @@ class RealAgnosticResidualInteractionBlock(_InteractionBase):
             mji = self.conv_tp(node_feats[sender], edge_attrs, tp_weights)
             message = scatter_sum(mji, receiver, num_nodes)
         message = self.linear(message) / self.avg_num_neighbors
-        return reshape_irreps(message, self.irreps_out), sc
+        return self.reshape(message), sc
 
 
 interaction_classes = {
@@ -255,9 +277,7 @@ class ScaleShiftMACE(torch.nn.Module):
         node_e0 = node_attrs @ self.atomic_energies
         e0 = scatter_sum(node_e0, batch, num_graphs)
         node_feats = self.node_embedding(node_attrs)
-        sender, receiver = edge_index[0], edge_index[1]
-        vectors = positions[receiver] - positions[sender] + shifts
-        lengths = vectors.norm(dim=-1, keepdim=True)
+        vectors, lengths = get_edge_vectors_and_lengths(positions=positions, edge_index=edge_index, shifts=shifts)
         edge_attrs = self.spherical_harmonics(vectors)
         edge_feats = self.radial_embedding(lengths)
         node_es = 0.0

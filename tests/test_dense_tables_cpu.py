@@ -134,3 +134,21 @@ def test_mlp_packed_hidden_weights():
     for W, z in zip(reversed(Ws), reversed(zs)):
         gg = (gg * c * dsilu(z)) @ W.T
     assert np.abs(gg - gx.numpy()).max() < 1e-5 * np.abs(gx.numpy()).max()
+
+
+def test_reshape_irreps_column_tables_match_the_module():
+    """CudaReshapeIrreps' gather tables applied on the host equal MACE's reshape_irreps, and the backward table is
+    the inverse permutation."""
+    import torch
+    from mace_mps_kernels_b200.dense import CudaReshapeIrreps, reshape_supported
+    from mace_mps_kernels_b200.standin import o3
+    from mace_mps_kernels_b200.standin.modules import reshape_irreps
+    for irreps in ('16x0e', '8x0e+8x1o+8x2e+8x3o', '4x1o+4x0e+4x2e'):
+        m = reshape_irreps(o3.Irreps(irreps))
+        assert reshape_supported(m) == (True, '')
+        op = CudaReshapeIrreps(m)
+        x = torch.randn(7, m.irreps.dim)
+        got = x[:, op.fwd_cols.long()].reshape(7, *op.shape)
+        assert torch.equal(got, m(x))
+        assert torch.equal(got.reshape(7, -1)[:, op.bwd_cols.long()], x)
+    assert not reshape_supported(reshape_irreps(o3.Irreps('8x0e+4x1o')))[0]

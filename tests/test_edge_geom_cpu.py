@@ -98,3 +98,38 @@ def test_edge_geometry_matches_model_modules(tmp_path):
     assert np.abs(rad[:, :8] - ref).max() < 2e-5 * np.abs(ref).max()
     assert np.abs(rad[:, 8] - gl.numpy()[:, 0]).max() < 2e-5 * np.abs(gl.numpy()).max()
     assert np.all(rad[-1] == 0.0)                            # beyond the cutoff: no feature, no gradient
+
+
+def test_edge_vector_patch_is_scoped_to_patched_models():
+    """patch_edge_vectors replaces the model module's get_edge_vectors_and_lengths by a wrapper that takes the CUDA
+    path only inside a patched model's forward and for CUDA float32 inputs; everything else calls the original, so
+    on the CPU a patched model and an unpatched one give the same energies and forces."""
+    import copy
+    import numpy as np
+    import torch
+    from mace_mps_kernels_b200 import standin
+    from mace_mps_kernels_b200.edge import _ACTIVE, patch_edge_vectors
+    from mace_mps_kernels_b200.standin import modules
+    ref = standin.make_model('8x0e+8x1o', 2, 2, seed=0)
+    met = copy.deepcopy(ref)
+    before = modules.get_edge_vectors_and_lengths
+    try:
+        assert patch_edge_vectors(met) == (True, '')
+        wrapped = modules.get_edge_vectors_and_lengths
+        assert wrapped is not before and wrapped._mmk_original is before
+        assert patch_edge_vectors(met) == (True, '')                  # idempotent: no second wrapper, no second hook
+        assert modules.get_edge_vectors_and_lengths is wrapped
+        st = standin.pt100_co_h(seed=0)
+        b = standin.structure_batch([st], standin.ELEMENTS_PTCOH, 5.0)
+        outs = []
+        for m in (ref, met):
+            bb = dict(b)
+            bb['positions'] = b['positions'].clone().requires_grad_(True)
+            o = m(bb, compute_force=True)
+            outs.append((o['energy'].detach().numpy(), o['forces'].detach().numpy()))
+        assert _ACTIVE[0] == 0                                        # the hooks balanced
+        # (the CPU's threaded reductions vary by ~1e-9 from run to run, so not bit for bit)
+        np.testing.assert_allclose(outs[0][0], outs[1][0], rtol=1e-6, atol=0)
+        np.testing.assert_allclose(outs[0][1], outs[1][1], rtol=0, atol=1e-8)
+    finally:
+        modules.get_edge_vectors_and_lengths = before

@@ -127,3 +127,25 @@ def test_linears_need_frozen_weights(cuda):
     model = helpers.make_model().to(cuda)
     report = patch_model(model, verbose=False, linears=True)
     assert any('frozen weights only' in why for _, why in report['skipped'])
+
+
+@pytest.mark.parametrize('irreps,N', [('128x0e+128x1o+128x2e+128x3o', 168), ('32x0e+32x1o', 1001), ('16x0e', 5)])
+def test_reshape_irreps_matches_module(cuda, irreps, N):
+    """CudaReshapeIrreps (one column gather each way) against MACE's reshape_irreps: forward and input gradient are
+    pure data movement, so both are bit for bit."""
+    from mace_mps_kernels_b200.dense import CudaReshapeIrreps
+    from mace_mps_kernels_b200.standin import o3
+    from mace_mps_kernels_b200.standin.modules import reshape_irreps
+    m = reshape_irreps(o3.Irreps(irreps))
+    op = CudaReshapeIrreps(m).to(cuda)
+    x = torch.randn(N, m.irreps.dim, device=cuda)
+    outs = []
+    for mod in (m, op):
+        xx = x.clone().requires_grad_(True)
+        y = mod(xx)
+        g = torch.arange(y.numel(), device=cuda, dtype=torch.float32).reshape(y.shape)
+        (gx,) = torch.autograd.grad(y, xx, g)
+        outs.append((y.detach(), gx))
+    assert outs[0][0].shape == outs[1][0].shape
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1], outs[1][1])

@@ -58,7 +58,7 @@ def test_model_with_edge_features_matches_unpatched(cuda, config):
         pytest.skip(f'no config {config}')
     ref, met, report = helpers.pair(config, cuda, edge_features=True)
     assert not report['skipped'], report['skipped']
-    assert report['patched'][-2:] == ['spherical_harmonics', 'radial_embedding'], report
+    assert report['patched'][-3:] == ['spherical_harmonics', 'radial_embedding', 'get_edge_vectors_and_lengths'], report
     for s in (0, 1):
         st = helpers.make_structure(seed=s)
         E0, F0 = helpers.energy_forces(ref, st, cuda)
@@ -76,3 +76,61 @@ def test_edge_features_double_backward_raises(cuda):
     with pytest.raises(RuntimeError, match='double backward'):
         (g,) = torch.autograd.grad(op(v).square().sum(), v, create_graph=True)
         torch.autograd.grad(g.sum(), v)
+
+
+@pytest.mark.parametrize('shift_grad', [False, True])
+def test_edge_vectors_match_pytorch(cuda, shift_grad):
+    """mmk_edge_vectors_fwd / _bwd against MACE's get_edge_vectors_and_lengths under autograd: vectors bit for bit,
+    lengths to 1 ulp, the position gradient (per-node sums over the receiver and sender CSRs) and the shift gradient
+    to float32 rounding.  Includes zero-length edges (the padding edges of a fixed-capacity graph: node to itself,
+    zero shift), whose length gradient is 0 as in PyTorch's norm backward."""
+    from mace_mps_kernels_b200.edge import edge_vectors_and_lengths
+    from mace_mps_kernels_b200.standin.modules import get_edge_vectors_and_lengths
+    rng = np.random.default_rng(7)
+    N, E = 300, 9000
+    pos = torch.tensor(rng.uniform(0, 12, (N, 3)), dtype=torch.float32, device=cuda)
+    ei = torch.tensor(np.stack([rng.integers(0, N, E), rng.integers(0, N, E)]), device=cuda)
+    ei[1, :50] = ei[0, :50]                                             # zero-length edges
+    sh = torch.tensor(rng.choice([-3.6, 0.0, 3.6], (E, 3)), dtype=torch.float32, device=cuda)
+    sh[:50] = 0.0
+    gv = torch.randn(E, 3, device=cuda)
+    gl = torch.randn(E, 1, device=cuda)
+    outs = []
+    for fn in (get_edge_vectors_and_lengths, None):
+        p = pos.clone().requires_grad_(True)
+        s = sh.clone().requires_grad_(shift_grad)
+        if fn is None:
+            v, ln = edge_vectors_and_lengths(p, ei.contiguous(), s)
+        else:
+            v, ln = fn(positions=p, edge_index=ei, shifts=s)
+        grads = torch.autograd.grad((v, ln), (p, s) if shift_grad else (p,), (gv, gl))
+        outs.append((v.detach(), ln.detach()) + tuple(g.detach() for g in grads))
+    (v0, l0, *g0), (v1, l1, *g1) = outs
+    assert torch.equal(v0, v1)
+    assert (l0 - l1).abs().max().item() <= 1e-6 * l0.abs().max().item()
+    assert float(l1[:50].abs().max()) == 0.0
+    for a, b in zip(g0, g1):
+        assert (a - b).abs().max().item() <= 2e-6 * a.abs().max().item()
+
+
+def test_patched_model_routes_edge_vectors_to_cuda(cuda):
+    """With edge_features=True the patched model's forward runs the fused edge-vector op (one launch each way) and
+    matches the unpatched model; the unpatched model keeps calling PyTorch's version."""
+    import copy
+    from mace_mps_kernels_b200 import _lib, patch_model
+    from mace_mps_kernels_b200 import standin as S
+    ref = S.make_model('32x0e+32x1o', 3, 2, seed=0, elements=S.ELEMENTS_PTCOH).to(cuda).requires_grad_(False)
+    met = copy.deepcopy(ref)
+    rep = patch_model(met, verbose=False, edge_features=True)
+    assert 'get_edge_vectors_and_lengths' in rep['patched']
+    b = S.to_device(S.structure_batch([S.pt100_co_h(seed=0)], S.ELEMENTS_PTCOH, 5.0), cuda)
+    res = []
+    for m in (ref, met):
+        n0 = _lib.LAUNCHES['mmk_edge_vectors_fwd']
+        bb = dict(b)
+        bb['positions'] = b['positions'].clone().requires_grad_(True)
+        o = m(bb, compute_force=True)
+        res.append((o['energy'].double().cpu(), o['forces'].double().cpu(), _lib.LAUNCHES['mmk_edge_vectors_fwd'] - n0))
+    assert res[0][2] == 0 and res[1][2] == 1
+    assert (res[0][0] - res[1][0]).abs().max().item() < E_ABS
+    assert (res[0][1] - res[1][1]).abs().max().item() < F_ABS
