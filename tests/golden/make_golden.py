@@ -1,4 +1,5 @@
-"""Generate the golden fixtures in this directory from the reference itself (run where /root/reference exists).
+"""Generate the golden fixtures in this directory from the reference itself (run where the reference sources are
+present: a sibling ``reference/src`` checkout, or the directory named by MMK_REFERENCE_SRC).
 
   python tests/golden/make_golden.py
 
