@@ -408,10 +408,11 @@ constexpr int smem_bytes() {
     return STAGES * (2 * BM * BK * 4 + 2 * BN * BK * 4) + STAGES * 8 + 16 + 1024;
 }
 
-// K splits of a launch: enough CTAs to cover the SMs when the output has few tiles, at least 4 chunks per split.
+// K splits of a launch when the output has few tiles: as many as keep tiles x splits within one wave (one CTA per SM:
+// a second, partial wave would double the launch), at least 4 chunks per split.
 inline int gemm_splits(long long tiles, int nk, int sms) {
     if (tiles >= sms || nk < 8) return 1;
-    long long s = (sms + tiles - 1) / tiles;
+    long long s = sms / tiles;
     s = s < nk / 4 ? s : nk / 4;
     return (int)(s < 1 ? 1 : (s > 16 ? 16 : s));
 }
