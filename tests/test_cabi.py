@@ -173,6 +173,11 @@ def test_gemm_entry_points_validate_arguments():
     assert L.mmk_gemm_tf32x3(None, 64, p, p, 64, p, 64, 10, 8, 64, None, 0, None) == _lib.MMK_ERR_INVALID
     assert L.mmk_gemm_tf32x3(p, 64, p, p, 64, p, 64, 0, 8, 64, None, 0, None) == _lib.MMK_OK              # empty
     assert L.mmk_gemm_workspace_bytes(5218, 64, 1280) > 0 and L.mmk_gemm_workspace_bytes(5218, 1280, 64) == 0
+    # K splits stay within one wave of CTAs (148 SMs without a GPU, one CTA per SM): 41 row tiles x 3 splits, not 4;
+    # the workspace is the 1 KB counter block plus the partial tiles (128 x 64 floats each)
+    assert L.mmk_gemm_workspace_bytes(5218, 64, 1280) == 1024 + 3 * 41 * 128 * 64 * 4
+    assert L.mmk_gemm_workspace_bytes(5218, 64, 512) == 1024 + 3 * 41 * 128 * 64 * 4
+    assert L.mmk_gemm_workspace_bytes(200 * 128, 64, 1280) == 0        # more tiles than SMs: no split
     assert L.mmk_tf32_split(p, p, p, -1, None) == _lib.MMK_ERR_INVALID
 
 
