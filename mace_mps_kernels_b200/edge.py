@@ -196,7 +196,14 @@ class _EdgeVectorsFn(torch.autograd.Function):
 
 def edge_vectors_and_lengths(positions, edge_index, shifts):
     """CUDA drop-in for MACE's ``get_edge_vectors_and_lengths(positions, edge_index, shifts)`` (normalize=False):
-    float32 CUDA positions and shifts, a contiguous int64 [2, E] edge_index."""
+    float32 CUDA positions [N, 3] and shifts [E, 3], a contiguous int64 [2, E] edge_index on the same device."""
+    if edge_index.dtype != torch.int64 or edge_index.dim() != 2 or edge_index.shape[0] != 2:
+        raise ValueError(f'edge_index must be int64 [2, E] (got {edge_index.dtype} {tuple(edge_index.shape)})')
+    if not edge_index.is_contiguous() or edge_index.device != positions.device:
+        raise ValueError('edge_index must be contiguous and on the positions\' device')
+    if positions.dim() != 2 or positions.shape[1] != 3 or shifts.shape != (edge_index.shape[1], 3):
+        raise ValueError(f'positions must be [N, 3] and shifts [E, 3] (got {tuple(positions.shape)}, '
+                         f'{tuple(shifts.shape)})')
     return _EdgeVectorsFn.apply(positions, shifts, edge_index)
 
 
@@ -239,6 +246,6 @@ def patch_edge_vectors(model):
         setattr(mod, 'get_edge_vectors_and_lengths', _fused_get_edge_vectors_and_lengths(fn))
     if not getattr(model, '_mmk_edge_vectors', False):
         model.register_forward_pre_hook(_enter)
-        model.register_forward_hook(_leave)
+        model.register_forward_hook(_leave, always_call=True)      # also when the forward raises
         model._mmk_edge_vectors = True
     return True, ''

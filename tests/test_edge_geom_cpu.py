@@ -128,8 +128,26 @@ def test_edge_vector_patch_is_scoped_to_patched_models():
             o = m(bb, compute_force=True)
             outs.append((o['energy'].detach().numpy(), o['forces'].detach().numpy()))
         assert _ACTIVE[0] == 0                                        # the hooks balanced
+        bad = dict(b)
+        del bad['shifts']
+        with pytest.raises(KeyError):
+            met(bad, compute_force=False)
+        assert _ACTIVE[0] == 0                                        # ... also when the forward raises
         # (the CPU's threaded reductions vary by ~1e-9 from run to run, so not bit for bit)
         np.testing.assert_allclose(outs[0][0], outs[1][0], rtol=1e-6, atol=0)
         np.testing.assert_allclose(outs[0][1], outs[1][1], rtol=0, atol=1e-8)
     finally:
         modules.get_edge_vectors_and_lengths = before
+
+
+def test_edge_vectors_argument_errors():
+    """The fused edge-vector op rejects what its kernel cannot read, before anything is launched (no GPU needed)."""
+    import torch
+    from mace_mps_kernels_b200.edge import edge_vectors_and_lengths
+    pos, sh = torch.zeros(4, 3), torch.zeros(5, 3)
+    with pytest.raises(ValueError, match='int64'):
+        edge_vectors_and_lengths(pos, torch.zeros(2, 5, dtype=torch.int32), sh)
+    with pytest.raises(ValueError, match='contiguous'):
+        edge_vectors_and_lengths(pos, torch.zeros(5, 2, dtype=torch.int64).t(), sh)
+    with pytest.raises(ValueError, match='shifts'):
+        edge_vectors_and_lengths(pos, torch.zeros(2, 5, dtype=torch.int64), torch.zeros(4, 3))
