@@ -9,7 +9,8 @@ rank runs its own structure (seed = rank): weak scaling, the only collective is 
 
 One step = one energy + force call (model forward + autograd backward through the patched kernels).  The model is
 patched with patch_model(model, edge_features=True, linears=True) on frozen weights: the reference's two ops (conv,
-symmetric contraction) plus this repository's edge-geometry, equivariant-linear and radial-MLP kernels.  Inputs are
+symmetric contraction) plus this repository's edge-geometry (edge vectors and lengths, spherical harmonics, radial
+basis), equivariant-linear, reshape and radial-MLP kernels.  Inputs are
 much smaller than L2, so L2 is flushed (256 MB write) before every timed step, outside the CUDA-event interval.
 
 The timed step is a replay of the whole E+F call captured in a CUDA graph (GraphedEnergyForces); the eager time is
