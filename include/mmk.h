@@ -123,6 +123,15 @@ MMK_API size_t mmk_csr_workspace_bytes(int64_t n_nodes, int64_t n_edges);
 MMK_API int mmk_csr_build(const int64_t *index, int64_t n_edges, int64_t n_nodes, int32_t *rowptr, int32_t *eids,
                   void *workspace, size_t workspace_bytes, int32_t *error_flag, void *stream);
 
+/* Both CSRs of an edge index in one sequence of launches (4 kernels and a memset instead of 2 x (4 kernels, a memset
+ * and a copy)): rowptr [2][n+1] and eids [2][E], row 0 the CSR of edge_index[0] (senders), row 1 of edge_index[1]
+ * (receivers), each row equal to mmk_csr_build of that index row.  edge_index: device int64 [2][E]; workspace:
+ * mmk_csr_pair_workspace_bytes() bytes, 16-byte aligned.  Sizes below 2^30. */
+MMK_API size_t mmk_csr_pair_workspace_bytes(int64_t n_nodes, int64_t n_edges);
+MMK_API int mmk_csr_build_pair(const int64_t *edge_index, int64_t n_edges, int64_t n_nodes, int32_t *rowptr,
+                               int32_t *eids, void *workspace, size_t workspace_bytes, int32_t *error_flag,
+                               void *stream);
+
 /* Same result as mmk_csr_build, for callers that cannot allocate device memory: an MD engine or plugin host that
  * owns every device allocation through its own pool and hands this library only its inputs and outputs, or code
  * that must not call cudaMalloc where it runs.  This entry point has no counterpart in the reference (which always
@@ -132,8 +141,9 @@ MMK_API int mmk_csr_build(const int64_t *index, int64_t n_edges, int64_t n_nodes
  *   MMK_ERR_INVALID without launching anything.
  * The first call on a device looks up that device's copy of the array (cudaGetSymbolAddress); make it before any
  * stream capture.  The address is remembered together with the device's current context and looked up again when
- * that context changes (after cudaDeviceReset, for instance); that call is then again a first call.  All calls share the one array: calls that overlap on the GPU (different streams, or threads)
- * race and must be serialised by the caller.  The array keeps the last call's contents; everything a call reads
+ * that context changes (after cudaDeviceReset, for instance); that call is then again a first call.  All calls share
+ * the one array: calls that overlap on the GPU (different streams, or threads) race and must be serialised by the
+ * caller.  The array keeps the last call's contents; everything a call reads
  * from it is written first by the same call. */
 #define MMK_NOALLOC_MAX_NODES (1 << 18)
 #define MMK_NOALLOC_MAX_EDGES (1 << 22)

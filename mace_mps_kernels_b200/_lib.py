@@ -51,6 +51,8 @@ SIGNATURES = {
     'mmk_conv_bwd': (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p]),
     'mmk_csr_workspace_bytes': (_sz, [_i64, _i64]),
     'mmk_csr_build': (_i, [_p, _i64, _i64, _p, _p, _p, _sz, _p, _p]),
+    'mmk_csr_pair_workspace_bytes': (_sz, [_i64, _i64]),
+    'mmk_csr_build_pair': (_i, [_p, _i64, _i64, _p, _p, _p, _sz, _p, _p]),
     'mmk_csr_build_noalloc': (_i, [_p, _i64, _i64, _p, _p, _p, _p]),
     'mmk_sc_layer_create': (_i, [ctypes.POINTER(SCDesc), ctypes.POINTER(_p)]),
     'mmk_sc_layer_destroy': (_i, [_p]),
@@ -113,7 +115,7 @@ def check(code):
 
 # kernels each entry point launches (bench.py reports the count issued inside its timed region)
 KERNELS_PER_CALL = {'mmk_conv_fwd': 1, 'mmk_conv_bwd': 1, 'mmk_sc_fwd': 1, 'mmk_sc_bwd': 1, 'mmk_csr_build': 4,
-                    'mmk_csr_build_noalloc': 4, 'mmk_elem_index': 1, 'mmk_elem_groups': 3,
+                    'mmk_csr_build_noalloc': 4, 'mmk_csr_build_pair': 4, 'mmk_elem_index': 1, 'mmk_elem_groups': 3,
                     'mmk_sh_fwd': 1, 'mmk_sh_bwd': 1, 'mmk_radial_fwd': 1, 'mmk_radial_bwd': 1,
                     'mmk_block_linear': 1, 'mmk_block_linear_act': 1, 'mmk_mlp_fwd': 1, 'mmk_mlp_bwd': 1,
                     'mmk_neighbor_list': 10, 'mmk_tf32_split': 1, 'mmk_gemm_tf32x3': 1,

@@ -198,6 +198,19 @@ def csr_build(index: torch.Tensor, n_nodes: int):
     return rowptr, eids
 
 
+def csr_build_pair(edge_index: torch.Tensor, n_nodes: int):
+    """(recv_rowptr, recv_eids, send_rowptr, send_eids) of a contiguous int64 [2, E] edge_index in one sequence of
+    launches (C ABI ``mmk_csr_build_pair``); each equals ``csr_build`` of that row."""
+    E = edge_index.shape[1]
+    rowptr = torch.empty(2, n_nodes + 1, dtype=torch.int32, device=edge_index.device)
+    eids = torch.empty(2, E, dtype=torch.int32, device=edge_index.device)
+    ws_bytes = _lib.lib().mmk_csr_pair_workspace_bytes(n_nodes, E)
+    ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=edge_index.device)
+    _lib.call('mmk_csr_build_pair', _lib.ptr(edge_index), E, n_nodes, _lib.ptr(rowptr), _lib.ptr(eids), _lib.ptr(ws),
+              ws_bytes, None, _lib.stream_of(edge_index))
+    return rowptr[1], eids[1], rowptr[0], eids[0]
+
+
 def graph_csr(edge_index: torch.Tensor, n_nodes: int):
     """Receiver and sender CSRs of a contiguous int64 [2, E] edge_index.  Both interaction layers and the backward of
     one evaluation see the same edge_index tensor, so the CSRs are built once and cached, keyed on the tensor object,
@@ -206,9 +219,7 @@ def graph_csr(edge_index: torch.Tensor, n_nodes: int):
     for ref, k, csr in reversed(_CSR_CACHE):
         if ref() is edge_index and k == key:
             return csr
-    recv = edge_index[1]
-    send = edge_index[0]
-    csr = csr_build(recv, n_nodes) + csr_build(send, n_nodes)
+    csr = csr_build_pair(edge_index, n_nodes)
     _CSR_CACHE.append((weakref.ref(edge_index), key, csr))
     del _CSR_CACHE[:-_CSR_CACHE_SIZE]
     return csr

@@ -130,6 +130,24 @@ def test_csr_matches_stable_argsort(cuda, N, E, seed):
     assert np.array_equal(eids.cpu().numpy(), e0)
 
 
+@pytest.mark.parametrize('N,E,seed', [(1, 0, 0), (7, 50, 1), (1000, 40000, 2), (300, 2, 3), (5000, 150000, 4)])
+def test_csr_pair_matches_stable_argsort_of_each_row(cuda, N, E, seed):
+    """mmk_csr_build_pair (both CSRs of an edge_index in one launch sequence) equals the oracle's csr_by of the
+    receiver row and of the sender row, bit for bit (including empty graphs, empty nodes and very long segments)."""
+    from mace_mps_kernels_b200.conv import csr_build_pair
+    rng = np.random.default_rng(seed)
+    ei = rng.integers(0, N, (2, E))
+    if seed == 2:
+        ei[1] = np.repeat(np.arange(N), E // N)[rng.permutation(E)]
+    if seed == 4:
+        ei[0, : E // 30] = 0                                     # one sender with 5 000 edges
+    rr, re, sr, se = csr_build_pair(torch.from_numpy(ei).to(cuda).contiguous(), N)
+    for (rowptr, eids), row in (((rr, re), ei[1]), ((sr, se), ei[0])):
+        r0, e0 = conv_ref.csr_by(row, N)
+        assert np.array_equal(rowptr.cpu().numpy(), r0)
+        assert np.array_equal(eids.cpu().numpy(), e0)
+
+
 @pytest.mark.parametrize('N,n_elem,seed', [(5, 4, 0), (1000, 1, 1), (70000, 3, 2), (257, 89, 3)])
 def test_elem_groups_match_stable_argsort(cuda, N, n_elem, seed):
     """Nodes grouped by element = a stable argsort of the element index (long segments: one element can hold every
