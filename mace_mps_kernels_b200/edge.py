@@ -177,6 +177,10 @@ class _EdgeVectorsFn(torch.autograd.Function):
         E, N = vec.shape[0], ctx.n_nodes
         if gvec is None and glen is None:
             return None, None, None
+        if E == 0:                                     # no edges: nothing reaches the positions or the shifts
+            gpos = torch.zeros(N, 3, device=vec.device) if ctx.needs_input_grad[0] else None
+            gsh = torch.zeros(0, 3, device=vec.device) if ctx.needs_input_grad[1] else None
+            return gpos, gsh, None
         gvec = gvec.contiguous() if gvec is not None else None
         glen = glen.contiguous() if glen is not None else None
         gpos = gsh = None
