@@ -310,7 +310,7 @@ class _GatherColumnsFn(torch.autograd.Function):
         N, D = xc.shape
         out = torch.empty((N,) + tuple(shape), device=xc.device, dtype=torch.float32)
         _lib.call('mmk_gather_columns', _lib.ptr(xc), D, _lib.ptr(out), D, _lib.ptr(fwd), N, D, _lib.stream_of(xc))
-        ctx.bwd = bwd
+        ctx.bwd, ctx.D = bwd, D
         return out
 
     @staticmethod
@@ -318,8 +318,7 @@ class _GatherColumnsFn(torch.autograd.Function):
         if torch.is_grad_enabled():
             raise RuntimeError(DOUBLE_BACKWARD_MSG)
         gc = g.contiguous()
-        N = gc.shape[0]
-        D = gc.numel() // max(N, 1)
+        N, D = gc.shape[0], ctx.D
         gx = torch.empty(N, D, device=gc.device, dtype=torch.float32)
         _lib.call('mmk_gather_columns', _lib.ptr(gc), D, _lib.ptr(gx), D, _lib.ptr(ctx.bwd), N, D, _lib.stream_of(gc))
         return gx, None, None, None
