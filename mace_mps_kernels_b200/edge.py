@@ -1,15 +1,18 @@
-"""MACE's per-edge geometry on B200: spherical harmonics of the edge vectors and the radial embedding of the edge
-lengths, each one CUDA kernel forward and one backward (C ABI ``mmk_sh_*`` / ``mmk_radial_*``).
+"""MACE's per-edge geometry on B200: the edge vectors and lengths, the spherical harmonics of the vectors and the
+radial embedding of the lengths, each one CUDA kernel forward and one backward (C ABI ``mmk_edge_vectors_*``,
+``mmk_sh_*``, ``mmk_radial_*``).
 
 In the reference these stay on e3nn / PyTorch, where they are a few dozen small elementwise kernels per call in each
 direction; at the graph sizes of an MD step (thousands of edges) those launches, not the arithmetic, set their cost.
 ``patch_model(model, edge_features=True)`` swaps ``model.spherical_harmonics`` and ``model.radial_embedding`` for
-the modules below.  Same definitions and outputs as the modules they replace (see ``csrc/edge_geom.cuh``); first-order
+the modules below and routes the model's ``get_edge_vectors_and_lengths`` calls to ``edge_vectors_and_lengths``
+(``patch_edge_vectors``).  Same definitions and outputs as the modules they replace (see ``csrc/edge_geom.cuh``); first-order
 backward only, double backward raises like the other patched ops.
 """
 from __future__ import annotations
 
 import ctypes
+import inspect
 
 import torch
 
@@ -246,6 +249,12 @@ def patch_edge_vectors(model):
     fn = getattr(mod, 'get_edge_vectors_and_lengths', None) if mod is not None else None
     if not callable(fn):
         return False, 'the model forward does not call get_edge_vectors_and_lengths from its module'
+    try:
+        calls = 'get_edge_vectors_and_lengths' in inspect.getsource(type(model).forward)
+    except (OSError, TypeError):
+        calls = False
+    if not calls:
+        return False, 'the model forward does not call get_edge_vectors_and_lengths itself'
     if not hasattr(fn, '_mmk_original'):
         setattr(mod, 'get_edge_vectors_and_lengths', _fused_get_edge_vectors_and_lengths(fn))
     if not getattr(model, '_mmk_edge_vectors', False):

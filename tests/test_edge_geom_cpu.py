@@ -151,3 +151,16 @@ def test_edge_vectors_argument_errors():
         edge_vectors_and_lengths(pos, torch.zeros(5, 2, dtype=torch.int64).t(), sh)
     with pytest.raises(ValueError, match='shifts'):
         edge_vectors_and_lengths(pos, torch.zeros(2, 5, dtype=torch.int64), torch.zeros(4, 3))
+
+
+def test_edge_vector_patch_skips_models_that_do_not_call_the_function():
+    """A model whose forward does not call get_edge_vectors_and_lengths itself is reported as skipped, not patched."""
+    import torch
+    from mace_mps_kernels_b200.edge import patch_edge_vectors
+
+    class Other(torch.nn.Module):
+        def forward(self, x):
+            return x
+
+    ok, why = patch_edge_vectors(Other())
+    assert not ok and 'get_edge_vectors_and_lengths' in why
